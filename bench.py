@@ -1,0 +1,384 @@
+"""Benchmark of the B200 neighbor-list provider (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg5]
+    python bench.py --impl reference ...     # reference CPU arm
+
+Workload (default cfg5, tonari_b200/workloads.py): 8192 triclinic structures,
+50-5000 atoms, mixed pbc, float32, cutoff 5, half list, 'PS'.  Scaling is
+weak: rank r processes its own seeded cfg5 batch (seed 5 + r), with no
+collective on the data path; value = pairs of all ranks / max-over-ranks time.
+
+A step is one neighbor_list call over the whole batch.
+* value: inputs already in HBM, device time per step from CUDA events on the
+  launching stream; L2 is flushed (256 MiB write) between steps, outside the
+  events.
+* e2e: the same call from pinned host inputs: H2D of positions/cell/pbc/
+  batch_ptr, the call, and D2H of every output into pinned host memory.
+* roofline: algorithmic bytes (inputs read once + requested outputs written
+  once) over the write-pass kernel time measured by the library's phase
+  events during the timed steps, against MEASURED_PEAKS.json hbm_gbs; the
+  whole-call fraction is reported as call_frac.
+* cpu_baseline: the reference CPU core (oracle/_ref, else the C port) on a
+  bounded sample of the same workload, all host cores, rank 0 at N=1 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--workload", default="cfg5")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--extra", default="cfg4",
+                        help="comma list of extra configs measured at N=1 on rank 0")
+    return parser.parse_args()
+
+
+def peak_hbm():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_workload(name: str, rank: int):
+    from tonari_b200 import workloads
+
+    seeds = {"cfg1": 0, "cfg2": 2, "cfg3": 3, "cfg4": 4, "cfg5": 5}
+    return workloads.CONFIGS[name](seed=seeds[name] + rank)
+
+
+def call_kwargs(w):
+    return {
+        "algorithm": w.options.get("algorithm", "auto"),
+        "sorted": w.options.get("sorted", False),
+        "half_list": w.options.get("half_list", False),
+    }
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.process = None
+
+    def __enter__(self):
+        try:
+            self.process = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.process = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.process is not None:
+            self.process.terminate()
+            self.process.wait()
+
+    def summary(self):
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k] == "Active"})
+        loaded = [v for v in sm if v > 0.5 * max(sm)] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def core_library():
+    from tonari_b200._extensions import CORE_LIBRARY
+
+    lib = ctypes.CDLL(str(CORE_LIBRARY))
+    lib.tnr_last_launch_count.restype = ctypes.c_int64
+    lib.tnr_last_phase_times.restype = ctypes.c_int
+    lib.tnr_last_phase_times.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_int]
+    return lib
+
+
+def phase_times(lib):
+    buffer = (ctypes.c_float * 5)()
+    lib.tnr_last_phase_times(buffer, 5)
+    return list(buffer)
+
+
+def measure_device(w, steps, warmup, device):
+    """Device-resident inputs; per-step CUDA events; L2 flushed between steps."""
+    import torch
+
+    from tonari_b200 import neighbor_list
+
+    lib = core_library()
+    positions, cell, pbc, batch_ptr = w.torch_inputs(device)
+    kwargs = call_kwargs(w)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        out = neighbor_list(w.quantities, positions, cell, pbc, w.cutoff, batch_ptr, **kwargs)
+        del out
+    torch.cuda.synchronize(device)
+    os.environ["TONARI_B200_PHASE_TIMERS"] = "1"
+    step_ms, write_ms, launches, n_pairs = [], [], [], 0
+    try:
+        for _ in range(steps):
+            flush.zero_()
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            out = neighbor_list(w.quantities, positions, cell, pbc, w.cutoff, batch_ptr, **kwargs)
+            end.record(stream)
+            end.synchronize()
+            step_ms.append(start.elapsed_time(end))
+            write_ms.append(phase_times(lib)[4])
+            launches.append(int(lib.tnr_last_launch_count()))
+            n_pairs = int(out[0].shape[0])
+            del out
+    finally:
+        os.environ.pop("TONARI_B200_PHASE_TIMERS", None)
+    return {"step_ms": step_ms, "write_ms": write_ms, "launches": launches, "n_pairs": n_pairs}
+
+
+def measure_e2e(w, steps, warmup, device):
+    """Pinned host inputs -> H2D -> call -> D2H of every output, per step."""
+    import torch
+
+    from tonari_b200 import neighbor_list
+
+    kwargs = call_kwargs(w)
+    host = [torch.from_numpy(a).pin_memory() for a in (w.positions, w.cell, w.pbc, w.batch_ptr)]
+    stream = torch.cuda.current_stream(device)
+    sinks = None
+    times, h2d, d2h = [], sum(t.numel() * t.element_size() for t in host), 0
+    for step in range(warmup + steps):
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        positions, cell, pbc, batch_ptr = (t.to(device, non_blocking=True) for t in host)
+        out = neighbor_list(w.quantities, positions, cell, pbc, w.cutoff, batch_ptr, **kwargs)
+        if sinks is None or any(s.shape != o.shape for s, o in zip(sinks, out)):
+            sinks = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in out]
+        for s, o in zip(sinks, out):
+            s.copy_(o, non_blocking=True)
+        end.record(stream)
+        end.synchronize()
+        if step >= warmup:
+            times.append(start.elapsed_time(end))
+        d2h = sum(o.numel() * o.element_size() for o in out)
+        del out
+    return {"step_ms": times, "h2d": h2d, "d2h": d2h}
+
+
+def cpu_reference_rate(w, max_seconds=3.0):
+    """Reference CPU core on a bounded sample of the workload (first structures,
+    growing until one run takes about max_seconds).  Returns a dict."""
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    kind = "reference" if oracle.ref_available() else "port"
+    b = w.n_structures
+    count = max(1, b // 64) if b > 1 else 1
+    while True:
+        sample = w.shard(0, count) if b > 1 else w
+        start = time.perf_counter()
+        if kind == "reference":
+            pairs, _ = oracle.ref_neighbor_list(
+                sample.positions, sample.cell, sample.pbc, sample.cutoff, sample.batch_ptr,
+                half_list=w.options.get("half_list", False),
+                algorithm=w.options.get("algorithm", "auto"), threads=threads)
+        else:
+            pairs, _ = oracle.port_neighbor_list(
+                sample.positions, sample.cell, sample.pbc, sample.cutoff, sample.batch_ptr,
+                half_list=w.options.get("half_list", False))
+            threads = 1
+        seconds = time.perf_counter() - start
+        if seconds >= max_seconds or count >= b or kind == "port":
+            break
+        count = min(b, max(count + 1, int(count * max_seconds / max(seconds, 1e-3))))
+    return {"value": len(pairs) / seconds, "unit": "pairs/s", "cores": threads, "kind": kind,
+            "sample": f"{w.name} structures [0,{count}) of {b}: {sample.n_atoms} atoms, "
+                      f"{len(pairs)} pairs in {seconds:.2f} s",
+            "structures_per_s": count / seconds}
+
+
+def roofline(w, n_pairs, write_ms, step_ms):
+    from tonari_b200.workloads import algorithmic_bytes
+
+    peak, source = peak_hbm()
+    traffic_bytes = algorithmic_bytes(w, n_pairs)
+    achieved = traffic_bytes / (write_ms * 1e-3) / 1e9
+    call = traffic_bytes / (step_ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{source} hbm_gbs",
+            "kernel": "cell/brute write pass", "algorithmic_bytes": traffic_bytes,
+            "traffic": None, "call_achieved": round(call, 1), "call_frac": round(call / peak, 4)}
+
+
+def run_reference(args):
+    """Reference arm: the reference's CPU implementation, all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    w = make_workload(args.workload, 0)
+    rates, samples = [], None
+    for step in range(args.warmup + args.steps):
+        result = cpu_reference_rate(w, max_seconds=1.0)
+        if step >= args.warmup:
+            rates.append(result["value"])
+            samples = result
+    value = statistics.median(rates)
+    line = {
+        "impl": "reference", "metric": "pairs/s", "value": value, "unit": "pairs/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if w.positions.dtype == np.float32 else "f64", "data": "synthetic",
+        "config": {"workload": w.name, "structures": w.n_structures, "atoms": w.n_atoms,
+                   "cutoff": w.cutoff, "quantities": w.quantities, **call_kwargs(w)},
+        "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": samples["cores"],
+                         "kind": samples["kind"], "sample": samples["sample"]},
+        "e2e": {"value": value, "unit": "pairs/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "structures_per_s": samples["structures_per_s"],
+        "reference_available": oracle.ref_available(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    from tonari_b200._extensions import load_torch_cuda
+
+    load_torch_cuda()
+
+    w = make_workload(args.workload, rank)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    barrier()
+    with Clocks(local_rank) as clocks:
+        device_run = measure_device(w, args.steps, args.warmup, device)
+        barrier()
+    total_ms = max_over_ranks(sum(device_run["step_ms"]))
+    ms_per_step = total_ms / args.steps
+    pairs_all = sum_over_ranks(device_run["n_pairs"])
+    structures_all = sum_over_ranks(w.n_structures)
+    value = pairs_all / (ms_per_step * 1e-3)
+
+    e2e = None
+    if not args.no_e2e:
+        barrier()
+        e2e_run = measure_e2e(w, max(3, args.steps // 2), 2, device)
+        barrier()
+        e2e_ms = max_over_ranks(statistics.mean(e2e_run["step_ms"]))
+        e2e = {"value": pairs_all / (e2e_ms * 1e-3), "unit": "pairs/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(sum_over_ranks(e2e_run["h2d"])),
+               "d2h_bytes_per_step": int(sum_over_ranks(e2e_run["d2h"]))}
+
+    write_ms = statistics.median(device_run["write_ms"])
+    line = {
+        "metric": "pairs/s", "value": value, "unit": "pairs/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if w.positions.dtype == np.float32 else "f64", "data": "synthetic",
+        "config": {"workload": w.name, "structures_per_gpu": w.n_structures,
+                   "atoms_per_gpu": w.n_atoms, "cutoff": w.cutoff, "quantities": w.quantities,
+                   **call_kwargs(w), "pairs_per_step": int(pairs_all),
+                   "l2": "flushed between steps (256 MiB write)",
+                   "parallelism": f"{world} independent ranks, no data-path collective"},
+        "structures_per_s": structures_all / (ms_per_step * 1e-3),
+        "gpu_launches": int(sum(device_run["launches"])),
+        "roofline": roofline(w, device_run["n_pairs"], write_ms, ms_per_step),
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference_rate(w)
+    if rank == 0 and world == 1 and args.extra:
+        extras = {}
+        for name in filter(None, args.extra.split(",")):
+            xw = make_workload(name, 0)
+            run = measure_device(xw, max(3, args.steps // 2), 2, device)
+            ms = statistics.mean(run["step_ms"])
+            extras[name] = {"pairs_per_s": run["n_pairs"] / (ms * 1e-3),
+                            "structures_per_s": xw.n_structures / (ms * 1e-3),
+                            "ms_per_step": ms, "pairs": run["n_pairs"],
+                            "roofline": roofline(xw, run["n_pairs"],
+                                                 statistics.median(run["write_ms"]), ms)}
+        line["extra_configs"] = extras
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

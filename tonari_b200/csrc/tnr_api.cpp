@@ -1,0 +1,743 @@
+// Host scheduler behind the C ABI (include/tonari_b200.h).
+//
+// Replaces tonari csrc/torch/bindings_cuda.cpp:59-228 and the host drivers
+// neighbor_list_cuda_brute_force (csrc/torch/neighbors_cuda.cu:443-556) and
+// neighbor_list_cuda_cell (csrc/torch/neighbors_cell_cuda.cu:558-814).
+//
+// Differences in design (same results):
+//   * algorithm selection is per structure (brute force for small candidate
+//     counts, cell list otherwise) instead of one choice for the whole batch;
+//   * the cell list bins image copies into a CSR layout by histogram -> scan
+//     -> scatter instead of per-bin linked lists, and never falls back to an
+//     O(N^2) pass because a wrap is nonzero: its final test is the public
+//     displacement formula, like the reference CPU cell list;
+//   * pairs are written source-major by construction, so `sorted` costs
+//     nothing and no argsort runs;
+//   * host round trips: at most three small device->host reads (per-structure
+//     extents, ghost total, pair total), each a pinned-memory copy.
+#include "tonari_b200.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <limits>
+#include <string>
+#include <vector>
+
+#include "tnr_geometry.h"
+#include "tnr_launch.h"
+#include "tnr_plan.h"
+
+namespace tnr {
+namespace {
+
+// Auto rule: a structure whose per-source candidate count (atoms x images)
+// is at most this takes the brute-force kernel.
+constexpr int64_t kBruteCandidatesPerSource = 2048;
+// The reference's bin-layout safety limits (tonari csrc/core/neighbors_cpu.cpp:23-24).
+constexpr int64_t kMaximumDenseBins = int64_t{1} << 26;
+constexpr int64_t kMaximumBinsPerImage = 64;
+// Total bins of one call (memory guard across a batch).
+constexpr int64_t kMaximumTotalBins = int64_t{1} << 28;
+constexpr int kRoundoffFactor = 64;
+
+thread_local int64_t g_launches = 0;
+thread_local float g_phase_ms[5] = {0, 0, 0, 0, 0};
+
+struct CudaError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+void check_cuda(cudaError_t error, const char* what) {
+    if (error != cudaSuccess) {
+        throw CudaError(std::string(what) + ": " + cudaGetErrorString(error));
+    }
+}
+
+void check_launch(const char* what) {
+    ++g_launches;
+    check_cuda(cudaGetLastError(), what);
+}
+
+// ---- allocation ------------------------------------------------------------
+
+void* default_allocate(void*, size_t bytes, tnr_stream stream) {
+    void* pointer = nullptr;
+    if (cudaMallocAsync(&pointer, bytes, reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return pointer;
+}
+
+void default_release(void*, void* pointer, tnr_stream stream) {
+    cudaFreeAsync(pointer, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// Workspace buffers of one call, released in stream order when it returns.
+class Workspace {
+public:
+    Workspace(const tnr_allocator& allocator, cudaStream_t stream)
+        : allocator_(allocator), stream_(stream) {}
+    ~Workspace() {
+        for (void* pointer : buffers_) {
+            allocator_.release(allocator_.context, pointer,
+                               reinterpret_cast<tnr_stream>(stream_));
+        }
+    }
+    Workspace(const Workspace&) = delete;
+    Workspace& operator=(const Workspace&) = delete;
+
+    template <typename U>
+    U* get(size_t count) {
+        void* pointer = raw(std::max<size_t>(count * sizeof(U), 16));
+        return static_cast<U*>(pointer);
+    }
+    void* raw(size_t bytes) {
+        void* pointer = allocator_.allocate(allocator_.context, bytes,
+                                            reinterpret_cast<tnr_stream>(stream_));
+        if (pointer == nullptr) throw std::bad_alloc();
+        buffers_.push_back(pointer);
+        return pointer;
+    }
+    // Output buffers are not released by the workspace.
+    template <typename U>
+    U* output(size_t count) {
+        void* pointer = allocator_.allocate(allocator_.context,
+                                            std::max<size_t>(count * sizeof(U), 16),
+                                            reinterpret_cast<tnr_stream>(stream_));
+        if (pointer == nullptr) throw std::bad_alloc();
+        outputs_.push_back(pointer);
+        return static_cast<U*>(pointer);
+    }
+    void release_outputs() {
+        for (void* pointer : outputs_) {
+            allocator_.release(allocator_.context, pointer,
+                               reinterpret_cast<tnr_stream>(stream_));
+        }
+        outputs_.clear();
+    }
+    void keep_outputs() { outputs_.clear(); }
+
+private:
+    tnr_allocator allocator_;
+    cudaStream_t stream_;
+    std::vector<void*> buffers_;
+    std::vector<void*> outputs_;
+};
+
+// Pinned host staging, one growable buffer per host thread.  Every call
+// synchronises its stream before returning, so a later call never overwrites
+// bytes an earlier copy is still reading.
+class Pinned {
+public:
+    ~Pinned() {
+        if (data_) cudaFreeHost(data_);
+    }
+    char* reserve(size_t bytes) {
+        if (bytes > size_) {
+            if (data_) cudaFreeHost(data_);
+            data_ = nullptr;
+            size_ = 0;
+            const size_t grown = std::max<size_t>(bytes, 1 << 16);
+            check_cuda(cudaHostAlloc(reinterpret_cast<void**>(&data_), grown,
+                                     cudaHostAllocPortable), "cudaHostAlloc");
+            size_ = grown;
+        }
+        return data_;
+    }
+
+private:
+    char* data_ = nullptr;
+    size_t size_ = 0;
+};
+
+thread_local Pinned g_pinned;
+
+// Packs several host arrays into one pinned block and one device block, then
+// uploads them with a single copy.
+class Upload {
+public:
+    template <typename U>
+    size_t add(const U* data, size_t count) {
+        const size_t offset = (bytes_.size() + 255) / 256 * 256;
+        bytes_.resize(offset + std::max<size_t>(count * sizeof(U), 1));
+        if (count) std::memcpy(bytes_.data() + offset, data, count * sizeof(U));
+        return offset;
+    }
+    char* commit(Workspace& workspace, cudaStream_t stream, char* pinned_region) {
+        char* device = static_cast<char*>(workspace.raw(std::max<size_t>(bytes_.size(), 16)));
+        std::memcpy(pinned_region, bytes_.data(), bytes_.size());
+        check_cuda(cudaMemcpyAsync(device, pinned_region, bytes_.size(), cudaMemcpyHostToDevice,
+                                   stream), "upload");
+        return device;
+    }
+    size_t size() const { return bytes_.size(); }
+
+private:
+    std::vector<char> bytes_;
+};
+
+struct PhaseTimer {
+    bool enabled = false;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t events[6] = {};
+    int recorded = 0;
+    explicit PhaseTimer(cudaStream_t s) : stream(s) {
+        const char* flag = std::getenv("TONARI_B200_PHASE_TIMERS");
+        enabled = flag && flag[0] == '1';
+        for (float& value : g_phase_ms) value = 0.0f;
+        if (enabled) {
+            for (auto& event : events) cudaEventCreate(&event);
+        }
+    }
+    ~PhaseTimer() {
+        if (enabled) {
+            for (auto& event : events) cudaEventDestroy(event);
+        }
+    }
+    void mark(int index) {
+        if (enabled && index < 6) {
+            cudaEventRecord(events[index], stream);
+            recorded = std::max(recorded, index + 1);
+        }
+    }
+    void finish() {
+        if (!enabled || recorded < 2) return;
+        cudaEventSynchronize(events[recorded - 1]);
+        for (int k = 0; k + 1 < recorded && k < 5; ++k) {
+            cudaEventElapsedTime(&g_phase_ms[k], events[k], events[k + 1]);
+        }
+    }
+};
+
+}  // namespace
+}  // namespace tnr
+
+namespace tnr {
+namespace {
+
+// Host mirror of the device order keys (tnr_kernels.cuh order_key).
+int32_t host_key(float v) {
+    int32_t bits;
+    std::memcpy(&bits, &v, 4);
+    return bits >= 0 ? bits : bits ^ 0x7fffffff;
+}
+long long host_key(double v) {
+    long long bits;
+    std::memcpy(&bits, &v, 8);
+    return bits >= 0 ? bits : bits ^ 0x7fffffffffffffffLL;
+}
+float host_value(int32_t key, float) {
+    const int32_t bits = key >= 0 ? key : key ^ 0x7fffffff;
+    float v;
+    std::memcpy(&v, &bits, 4);
+    return v;
+}
+double host_value(long long key, double) {
+    const long long bits = key >= 0 ? key : key ^ 0x7fffffffffffffffLL;
+    double v;
+    std::memcpy(&v, &bits, 8);
+    return v;
+}
+
+template <typename T>
+Reduction<T> neutral_reduction() {
+    Reduction<T> r{};
+    for (int c = 0; c < 3; ++c) {
+        r.wrapped_min[c] = host_key(std::numeric_limits<T>::infinity());
+        r.wrapped_max[c] = host_key(-std::numeric_limits<T>::infinity());
+        r.position_abs_max[c] = host_key(T(0));
+        r.wrap_abs_max[c] = 0;
+    }
+    return r;
+}
+
+const char* kCannotSafely =
+    "cell_list cannot safely process this structure; use algorithm='auto' or 'brute_force'";
+
+enum class CellPlan { kReady, kUnsafe, kPreferBrute };
+
+// Cell-list plan of one structure from its reduced extents, following the
+// reference's safety rules (tonari csrc/core/neighbors_cpu.cpp:156-219 for the
+// padded search radius, :379-430 for the bin layout).  kUnsafe is the
+// reference's "cannot safely process" outcome; kPreferBrute marks inputs this
+// implementation routes to the brute-force kernel for its own reasons (output
+// shifts that could leave int32), with the same pair set.
+template <typename T>
+CellPlan plan_cell(StructurePlan<T>& plan, const Reduction<T>& reduction, const T* cell,
+               double cutoff) {
+    const T scalar_cutoff = static_cast<T>(cutoff);
+    T lo[3], hi[3];
+    long double scale = 0.0L;
+    for (int c = 0; c < 3; ++c) {
+        lo[c] = host_value(reduction.wrapped_min[c], T(0));
+        hi[c] = host_value(reduction.wrapped_max[c], T(0));
+        if (!std::isfinite(lo[c]) || !std::isfinite(hi[c])) return CellPlan::kUnsafe;
+        long double component =
+            2.0L * static_cast<long double>(host_value(reduction.position_abs_max[c], T(0)));
+        for (int a = 0; a < 3; ++a) {
+            const int64_t output_shift =
+                static_cast<int64_t>(plan.repeats[a]) + 2 * static_cast<int64_t>(reduction.wrap_abs_max[a]);
+            component += static_cast<long double>(output_shift) *
+                         std::abs(static_cast<long double>(cell[3 * a + c]));
+        }
+        scale = std::max(scale, component);
+    }
+    // Output shifts of cell-list pairs are image - wrap_t + wrap_s; keep them
+    // inside int32 so the search kernel needs no range test.
+    for (int a = 0; a < 3; ++a) {
+        const int64_t bound = static_cast<int64_t>(plan.repeats[a]) +
+                              2 * static_cast<int64_t>(reduction.wrap_abs_max[a]);
+        if (bound >= std::numeric_limits<int32_t>::max()) return CellPlan::kPreferBrute;
+    }
+    const long double padding = kRoundoffFactor * std::numeric_limits<T>::epsilon() * scale;
+    const long double padded = static_cast<long double>(scalar_cutoff) + padding;
+    if (!std::isfinite(static_cast<double>(padded)) || padded > 2 * static_cast<long double>(scalar_cutoff) ||
+        padded > std::numeric_limits<T>::max()) {
+        return CellPlan::kUnsafe;
+    }
+    const T search = std::nextafter(static_cast<T>(padded), std::numeric_limits<T>::infinity());
+    if (!std::isfinite(search)) return CellPlan::kUnsafe;
+    const T inner = std::max(T(0), 2 * scalar_cutoff - search);
+
+    // Reference bin layout test with bin edge = search radius.
+    int64_t count = 1;
+    int64_t dims0[3];
+    for (int c = 0; c < 3; ++c) {
+        const T span = hi[c] - lo[c] + 2 * search;
+        const T dimension = span / search;
+        if (!std::isfinite(dimension) || dimension > kMaximumDenseBins) return CellPlan::kUnsafe;
+        dims0[c] = std::max<int64_t>(1, static_cast<int64_t>(std::ceil(dimension)));
+        if (count > kMaximumDenseBins / dims0[c]) return CellPlan::kUnsafe;
+        count *= dims0[c];
+    }
+    const int64_t possible_images = static_cast<int64_t>(plan.n_atoms) * plan.n_images;
+    if ((count + kMaximumBinsPerImage - 1) / kMaximumBinsPerImage > possible_images) return CellPlan::kUnsafe;
+
+    // Actual grid: the edge is widened by a few ulps of the largest bin
+    // coordinate so that two points closer than the search radius can never
+    // land two bins apart after rounding.
+    const int64_t largest = std::max({dims0[0], dims0[1], dims0[2]}) + 2;
+    const double widen = 1.0 + 8.0 * std::numeric_limits<T>::epsilon() * static_cast<double>(largest);
+    const T edge = static_cast<T>(static_cast<double>(search) * widen);
+    plan.inv_edge = T(1) / edge;
+    for (int c = 0; c < 3; ++c) {
+        plan.origin[c] = lo[c] - search;
+        plan.lower[c] = lo[c] - search;
+        plan.upper[c] = hi[c] + search;
+        const T span = hi[c] - lo[c] + 2 * search;
+        int64_t dim = std::max<int64_t>(1, static_cast<int64_t>(std::ceil(span / edge)));
+        dim = std::min(dim, dims0[c]);
+        plan.dims[c] = static_cast<int32_t>(dim);
+    }
+    plan.search_squared = search * search;
+    plan.inner_squared = inner * inner;
+    return CellPlan::kReady;
+}
+
+template <typename T>
+void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
+         tnr_result& result) {
+    using V4 = typename std::conditional<std::is_same<T, float>::value, float4, double4>::type;
+    const int64_t n_atoms = request.n_atoms;
+    const int64_t batch = request.n_structures;
+    PhaseTimer timer(stream);
+
+    // ---- host metadata (tonari csrc/torch/bindings_cuda.cpp:96-131) -------
+    std::vector<int64_t> batch_ptr(static_cast<size_t>(batch + 1));
+    std::vector<T> cell_t(static_cast<size_t>(9 * batch));
+    std::vector<uint8_t> pbc(static_cast<size_t>(3 * batch));
+    if (request.batch_ptr_host && request.cell_host && request.pbc_host) {
+        std::memcpy(batch_ptr.data(), request.batch_ptr_host, batch_ptr.size() * sizeof(int64_t));
+        std::memcpy(cell_t.data(), request.cell_host, cell_t.size() * sizeof(T));
+        std::memcpy(pbc.data(), request.pbc_host, pbc.size());
+    } else {
+        const size_t b0 = batch_ptr.size() * sizeof(int64_t);
+        const size_t b1 = (cell_t.size() * sizeof(T) + 15) / 16 * 16;
+        char* staging = g_pinned.reserve(b0 + b1 + pbc.size() + 64);
+        check_cuda(cudaMemcpyAsync(staging, request.batch_ptr, b0, cudaMemcpyDeviceToHost, stream), "read batch_ptr");
+        if (batch) {
+            check_cuda(cudaMemcpyAsync(staging + b0, request.cell, cell_t.size() * sizeof(T),
+                                       cudaMemcpyDeviceToHost, stream), "read cell");
+            check_cuda(cudaMemcpyAsync(staging + b0 + b1, request.pbc, pbc.size(),
+                                       cudaMemcpyDeviceToHost, stream), "read pbc");
+        }
+        check_cuda(cudaStreamSynchronize(stream), "metadata read");
+        std::memcpy(batch_ptr.data(), staging, b0);
+        std::memcpy(cell_t.data(), staging + b0, cell_t.size() * sizeof(T));
+        std::memcpy(pbc.data(), staging + b0 + b1, pbc.size());
+    }
+    require_input(batch_ptr[0] == 0, "batch_ptr must start at zero");
+    require_input(batch_ptr[batch] == n_atoms, "batch_ptr must end at N_total");
+    std::vector<int64_t> counts(static_cast<size_t>(batch));
+    for (int64_t b = 0; b < batch; ++b) {
+        require_input(batch_ptr[b + 1] >= batch_ptr[b], "batch_ptr must be nondecreasing");
+        counts[b] = batch_ptr[b + 1] - batch_ptr[b];
+    }
+    for (uint8_t& flag : pbc) flag = flag ? 1 : 0;
+    std::vector<double> cell64(cell_t.begin(), cell_t.end());
+    const PeriodicGeometry geometry =
+        build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
+
+    result.n_pairs = 0;
+    if (n_atoms == 0) return;
+    timer.mark(0);
+
+    // One pinned block for every later upload and readback of this call; it
+    // is reserved once here, after the metadata copy above has completed.
+    const size_t prepare_bytes = static_cast<size_t>(batch) *
+        (sizeof(PrepareStructure<T>) + sizeof(Reduction<T>)) + 1024;
+    const size_t plan_bytes = static_cast<size_t>(batch) *
+        (sizeof(StructurePlan<T>) + 2 * sizeof(int64_t) + 2 * sizeof(int32_t)) + 4096;
+    const size_t read_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>) + 1024;
+    char* pinned = g_pinned.reserve(prepare_bytes + plan_bytes + read_bytes);
+    char* pinned_prepare = pinned;
+    char* pinned_plan = pinned + prepare_bytes;
+    char* pinned_read = pinned + prepare_bytes + plan_bytes;
+
+    // ---- prepare: wraps, wrapped positions, per-structure extents ---------
+    std::vector<PrepareStructure<T>> prepare(static_cast<size_t>(batch));
+    for (int64_t b = 0; b < batch; ++b) {
+        PrepareStructure<T>& st = prepare[b];
+        st.atom_begin = batch_ptr[b];
+        st.atom_end = batch_ptr[b + 1];
+        for (int k = 0; k < 9; ++k) {
+            st.cell[k] = cell_t[9 * b + k];
+            st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
+        }
+    }
+    std::vector<Reduction<T>> reductions(static_cast<size_t>(batch), neutral_reduction<T>());
+    Upload first;
+    const size_t off_prepare = first.add(prepare.data(), prepare.size());
+    const size_t off_reduction = first.add(reductions.data(), reductions.size());
+    char* first_device = first.commit(workspace, stream, pinned_prepare);
+    auto* d_prepare = reinterpret_cast<PrepareStructure<T>*>(first_device + off_prepare);
+    auto* d_reductions = reinterpret_cast<Reduction<T>*>(first_device + off_reduction);
+
+    int64_t* d_batch_ptr = const_cast<int64_t*>(request.batch_ptr);
+    if (d_batch_ptr == nullptr) {
+        throw InputError("batch_ptr device pointer is required");
+    }
+    auto* d_atom_struct = workspace.get<int32_t>(n_atoms);
+    auto* d_wraps = workspace.get<int32_t>(3 * n_atoms);
+    auto* d_wrapped = workspace.get<V4>(n_atoms);
+    auto* d_status = workspace.get<uint32_t>(4);
+    check_cuda(cudaMemsetAsync(d_status, 0, 4 * sizeof(uint32_t), stream), "memset status");
+
+    PrepareArgs<T> prepare_args{static_cast<const T*>(request.positions), n_atoms, d_batch_ptr,
+                                batch, d_prepare, d_atom_struct, d_wraps, d_wrapped,
+                                d_reductions, d_status};
+    launch_prepare(prepare_args, stream);
+    check_launch("prepare kernel");
+    timer.mark(1);
+
+    // ---- per-structure algorithm ----------------------------------------
+    std::vector<int32_t> mode(static_cast<size_t>(batch), kModeEmpty);
+    bool any_cell = false;
+    for (int64_t b = 0; b < batch; ++b) {
+        if (counts[b] == 0) continue;
+        const int64_t images = geometry.image_begin[b + 1] - geometry.image_begin[b];
+        bool cell = false;
+        if (request.algorithm == TNR_CELL_LIST) {
+            cell = true;
+        } else if (request.algorithm == TNR_AUTO) {
+            cell = counts[b] > kBruteCandidatesPerSource / std::max<int64_t>(images, 1);
+        }
+        mode[b] = cell ? kModeCell : kModeBrute;
+        any_cell = any_cell || cell;
+    }
+
+    auto check_status = [&](uint32_t status) {
+        require_search(!(status & kStatusNonFinite), "positions must contain only finite values");
+        require_search(!(status & kStatusWrapRange),
+                       "atom representatives require periodic wraps outside the int32 range");
+        require_search(!(status & kStatusShiftRange),
+                       "a cell shift required by the cutoff pairs exceeds the int32 output range");
+        require_search(!(status & kStatusScanTimeout),
+                       "a device-wide scan exceeded its bounded wait");
+        require_search(!(status & kStatusCapacity), "an internal capacity was exceeded");
+        require_search(!(status & kStatusCountRange),
+                       "a per-source pair count exceeds the int32 range");
+    };
+
+    std::vector<StructurePlan<T>> plans(static_cast<size_t>(batch));
+    for (int64_t b = 0; b < batch; ++b) {
+        StructurePlan<T>& plan = plans[b];
+        std::memset(&plan, 0, sizeof(plan));
+        plan.atom_begin = batch_ptr[b];
+        plan.n_atoms = static_cast<int32_t>(counts[b]);
+        plan.mode = mode[b];
+        plan.image_begin = geometry.image_begin[b];
+        plan.n_images = static_cast<int32_t>(geometry.image_begin[b + 1] - geometry.image_begin[b]);
+        for (int a = 0; a < 3; ++a) plan.repeats[a] = geometry.repeats[3 * b + a];
+        for (int k = 0; k < 9; ++k) plan.cell[k] = cell_t[9 * b + k];
+        plan.cutoff_squared = static_cast<T>(request.cutoff * request.cutoff);
+        plan.dims[0] = plan.dims[1] = plan.dims[2] = 1;
+    }
+
+    int64_t total_bins = 0;
+    if (any_cell) {
+        check_cuda(cudaMemcpyAsync(pinned_read, d_reductions, reductions.size() * sizeof(Reduction<T>),
+                                   cudaMemcpyDeviceToHost, stream), "read extents");
+        check_cuda(cudaMemcpyAsync(pinned_read + reductions.size() * sizeof(Reduction<T>), d_status,
+                                   sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "read status");
+        check_cuda(cudaStreamSynchronize(stream), "extents");
+        std::memcpy(reductions.data(), pinned_read, reductions.size() * sizeof(Reduction<T>));
+        uint32_t status = 0;
+        std::memcpy(&status, pinned_read + reductions.size() * sizeof(Reduction<T>), sizeof(status));
+        check_status(status);
+        for (int64_t b = 0; b < batch; ++b) {
+            if (mode[b] != kModeCell) continue;
+            StructurePlan<T>& plan = plans[b];
+            const CellPlan outcome =
+                plan_cell(plan, reductions[b], cell_t.data() + 9 * b, request.cutoff);
+            const int64_t bins = outcome == CellPlan::kReady
+                ? int64_t{plan.dims[0]} * plan.dims[1] * plan.dims[2] : 0;
+            if (outcome != CellPlan::kReady || total_bins + bins > kMaximumTotalBins) {
+                require_search(request.algorithm != TNR_CELL_LIST || outcome == CellPlan::kPreferBrute,
+                               kCannotSafely);
+                plan.mode = mode[b] = kModeBrute;
+                plan.dims[0] = plan.dims[1] = plan.dims[2] = 1;
+                continue;
+            }
+            plan.bin_begin = total_bins;
+            total_bins += bins;
+        }
+    }
+
+    // ---- work lists -------------------------------------------------------
+    std::vector<int32_t> cell_structs, brute_structs;
+    std::vector<int64_t> cell_prefix{0}, brute_prefix{0};
+    for (int64_t b = 0; b < batch; ++b) {
+        if (mode[b] == kModeCell) {
+            cell_structs.push_back(static_cast<int32_t>(b));
+            cell_prefix.push_back(cell_prefix.back() + counts[b]);
+        } else if (mode[b] == kModeBrute) {
+            brute_structs.push_back(static_cast<int32_t>(b));
+            brute_prefix.push_back(brute_prefix.back() + counts[b]);
+        }
+    }
+    const int64_t n_cell_atoms = cell_prefix.back();
+    const int64_t n_brute_atoms = brute_prefix.back();
+    Upload second;
+    const size_t off_plans = second.add(plans.data(), plans.size());
+    const size_t off_cell_prefix = second.add(cell_prefix.data(), cell_prefix.size());
+    const size_t off_cell_structs = second.add(cell_structs.data(), cell_structs.size());
+    const size_t off_brute_prefix = second.add(brute_prefix.data(), brute_prefix.size());
+    const size_t off_brute_structs = second.add(brute_structs.data(), brute_structs.size());
+    char* second_device = second.commit(workspace, stream, pinned_plan);
+    auto* d_plans = reinterpret_cast<StructurePlan<T>*>(second_device + off_plans);
+
+    // ---- cell list binning: histogram -> scan -> scatter ------------------
+    unsigned long long* d_bin_start = nullptr;
+    V4* d_ghost_pos = nullptr;
+    int4* d_ghost_meta = nullptr;
+    int32_t* d_self_slot = nullptr;
+    int32_t* d_source_list = nullptr;
+    const int64_t scan_items = std::max<int64_t>(n_atoms, total_bins);
+    void* d_scan_workspace = workspace.raw(scan_workspace_bytes(scan_items));
+    BinArgs<T> bin_args{};
+    bin_args.plans = d_plans;
+    bin_args.cell_prefix = reinterpret_cast<const int64_t*>(second_device + off_cell_prefix);
+    bin_args.cell_structs = reinterpret_cast<const int32_t*>(second_device + off_cell_structs);
+    bin_args.n_cell = static_cast<int32_t>(cell_structs.size());
+    bin_args.n_cell_atoms = n_cell_atoms;
+    bin_args.wraps = d_wraps;
+    bin_args.wrapped = d_wrapped;
+    bin_args.status = d_status;
+    if (n_cell_atoms > 0) {
+        auto* d_bin_counts = workspace.get<unsigned long long>(total_bins);
+        d_bin_start = workspace.get<unsigned long long>(total_bins + 1);
+        auto* d_cursor = workspace.get<unsigned long long>(total_bins + 1);
+        check_cuda(cudaMemsetAsync(d_bin_counts, 0, total_bins * sizeof(unsigned long long), stream),
+                   "memset bins");
+        bin_args.bin_counts = d_bin_counts;
+        launch_bin(bin_args, false, stream);
+        check_launch("bin histogram kernel");
+        launch_scan_u64(d_bin_counts, total_bins, d_bin_start, d_cursor, d_scan_workspace, d_status,
+                        stream);
+        check_launch("bin scan kernel");
+        unsigned long long packed_total = 0;
+        check_cuda(cudaMemcpyAsync(pinned_read, d_bin_start + total_bins, sizeof(packed_total),
+                                   cudaMemcpyDeviceToHost, stream), "read ghost total");
+        check_cuda(cudaStreamSynchronize(stream), "ghost total");
+        std::memcpy(&packed_total, pinned_read, sizeof(packed_total));
+        const int64_t ghosts = static_cast<int64_t>(packed_total & 0xffffffffull);
+        const int64_t sources = static_cast<int64_t>(packed_total >> 32);
+        require_search(sources == n_cell_atoms && ghosts >= sources &&
+                           ghosts < std::numeric_limits<int32_t>::max(),
+                       "cell-list image copies exceed int32 indexing");
+        d_ghost_pos = workspace.get<V4>(ghosts);
+        d_ghost_meta = workspace.get<int4>(ghosts);
+        d_self_slot = workspace.get<int32_t>(n_atoms);
+        d_source_list = workspace.get<int32_t>(n_cell_atoms);
+        bin_args.bin_counts = d_cursor;
+        bin_args.ghost_pos = d_ghost_pos;
+        bin_args.ghost_meta = d_ghost_meta;
+        bin_args.self_slot = d_self_slot;
+        bin_args.source_list = d_source_list;
+        launch_bin(bin_args, true, stream);
+        check_launch("bin scatter kernel");
+    }
+    timer.mark(2);
+
+    // ---- count pass -> scan -> exact E -------------------------------------
+    auto* d_counts = workspace.get<uint32_t>(n_atoms);
+    auto* d_pair_start = workspace.get<int64_t>(n_atoms + 1);
+    check_cuda(cudaMemsetAsync(d_counts, 0, n_atoms * sizeof(uint32_t), stream), "memset counts");
+    SearchArgs<T> search{};
+    search.positions = static_cast<const T*>(request.positions);
+    search.atom_struct = d_atom_struct;
+    search.wraps = d_wraps;
+    search.wrapped = d_wrapped;
+    search.plans = d_plans;
+    search.bin_start = d_bin_start;
+    search.ghost_pos = d_ghost_pos;
+    search.ghost_meta = d_ghost_meta;
+    search.self_slot = d_self_slot;
+    search.source_list = d_source_list;
+    search.n_sources = n_cell_atoms;
+    search.brute_prefix = reinterpret_cast<const int64_t*>(second_device + off_brute_prefix);
+    search.brute_structs = reinterpret_cast<const int32_t*>(second_device + off_brute_structs);
+    search.n_brute = static_cast<int32_t>(brute_structs.size());
+    search.n_brute_atoms = n_brute_atoms;
+    search.counts = d_counts;
+    search.pair_start = d_pair_start;
+    search.index_offset = request.index_offset;
+    search.status = d_status;
+    search.half_list = request.half_list ? 1 : 0;
+    search.include_self = request.include_self ? 1 : 0;
+    if (n_cell_atoms) {
+        launch_cell_search(search, false, stream);
+        check_launch("cell count kernel");
+    }
+    if (n_brute_atoms) {
+        launch_brute_search(search, false, stream);
+        check_launch("brute count kernel");
+    }
+    timer.mark(3);
+    launch_scan_counts(d_counts, n_atoms, d_pair_start, d_scan_workspace, d_status, stream);
+    check_launch("pair scan kernel");
+    timer.mark(4);
+    check_cuda(cudaMemcpyAsync(pinned_read, d_pair_start + n_atoms, sizeof(int64_t),
+                               cudaMemcpyDeviceToHost, stream), "read pair total");
+    check_cuda(cudaMemcpyAsync(pinned_read + sizeof(int64_t), d_status, sizeof(uint32_t),
+                               cudaMemcpyDeviceToHost, stream), "read status");
+    check_cuda(cudaStreamSynchronize(stream), "pair total");
+    int64_t n_pairs = 0;
+    uint32_t status = 0;
+    std::memcpy(&n_pairs, pinned_read, sizeof(n_pairs));
+    std::memcpy(&status, pinned_read + sizeof(int64_t), sizeof(status));
+    check_status(status);
+    require_search(n_pairs >= 0, "neighbor-list output exceeds the int64 range");
+
+    // ---- exact-size outputs and the write pass -----------------------------
+    result.n_pairs = n_pairs;
+    if (n_pairs == 0) return;
+    const uint32_t q = request.quantities;
+    const size_t e = static_cast<size_t>(n_pairs);
+    if (q & TNR_Q_I) result.i = workspace.output<int64_t>(e);
+    if (q & TNR_Q_J) result.j = workspace.output<int64_t>(e);
+    if (q & TNR_Q_P) result.P = workspace.output<int64_t>(2 * e);
+    if (q & TNR_Q_S) result.S = workspace.output<int32_t>(3 * e);
+    if (q & TNR_Q_d) result.d = workspace.output<T>(e);
+    if (q & TNR_Q_D) result.D = workspace.output<T>(3 * e);
+    search.out_i = result.i;
+    search.out_j = result.j;
+    search.out_P = result.P;
+    search.out_S = result.S;
+    search.out_d = static_cast<T*>(result.d);
+    search.out_D = static_cast<T*>(result.D);
+    if (q != 0) {
+        if (n_cell_atoms) {
+            launch_cell_search(search, true, stream);
+            check_launch("cell write kernel");
+        }
+        if (n_brute_atoms) {
+            launch_brute_search(search, true, stream);
+            check_launch("brute write kernel");
+        }
+    }
+    timer.mark(5);
+    timer.finish();
+}
+
+void set_message(char* message, size_t length, const char* text) {
+    if (message == nullptr || length == 0) return;
+    std::strncpy(message, text, length - 1);
+    message[length - 1] = '\0';
+}
+
+}  // namespace
+}  // namespace tnr
+
+extern "C" {
+
+int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator,
+                      tnr_stream stream_handle, tnr_result* result, char* message,
+                      size_t message_length) {
+    using namespace tnr;
+    if (request == nullptr || result == nullptr) {
+        set_message(message, message_length, "request and result must not be null");
+        return TNR_INPUT_ERROR;
+    }
+    *result = tnr_result{};
+    g_launches = 0;
+    tnr_allocator chosen{nullptr, default_allocate, default_release};
+    if (allocator && allocator->allocate && allocator->release) chosen = *allocator;
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_handle);
+    Workspace workspace(chosen, stream);
+    try {
+        require_input(std::isfinite(request->cutoff) && request->cutoff > 0,
+                      "cutoff must be finite and positive");
+        require_input(request->n_atoms >= 0 && request->n_structures >= 0,
+                      "batch_ptr must have shape (B + 1,)");
+        require_input(request->n_atoms < (int64_t{1} << 31),
+                      "the current implementation supports fewer than 2^31 atoms");
+        require_input(request->algorithm >= TNR_AUTO && request->algorithm <= TNR_CELL_LIST,
+                      "algorithm must be 'auto', 'brute_force', or 'cell_list'");
+        require_input(request->dtype == TNR_FLOAT32 || request->dtype == TNR_FLOAT64,
+                      "positions must have dtype float32 or float64");
+        tnr_result local{};
+        if (request->dtype == TNR_FLOAT32) {
+            run<float>(*request, workspace, stream, local);
+        } else {
+            run<double>(*request, workspace, stream, local);
+        }
+        workspace.keep_outputs();
+        *result = local;
+        return TNR_OK;
+    } catch (const InputError& error) {
+        workspace.release_outputs();
+        set_message(message, message_length, error.what());
+        return TNR_INPUT_ERROR;
+    } catch (const SearchError& error) {
+        workspace.release_outputs();
+        set_message(message, message_length, error.what());
+        return TNR_SEARCH_ERROR;
+    } catch (const std::bad_alloc&) {
+        workspace.release_outputs();
+        set_message(message, message_length, "device allocation failed");
+        return TNR_ALLOC_ERROR;
+    } catch (const std::exception& error) {
+        workspace.release_outputs();
+        set_message(message, message_length, error.what());
+        return TNR_CUDA_ERROR;
+    }
+}
+
+const char* tnr_version(void) { return "0.1.0"; }
+
+int64_t tnr_last_launch_count(void) { return tnr::g_launches; }
+
+int tnr_last_phase_times(float* times_ms, int capacity) {
+    const int count = std::min(capacity, 5);
+    for (int k = 0; k < count; ++k) times_ms[k] = tnr::g_phase_ms[k];
+    return count;
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Kernel launch interface used by the host scheduler (tnr_api.cpp).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "tnr_plan.h"
+
+namespace tnr {
+
+template <typename T>
+struct PrepareArgs {
+    const T* positions;
+    int64_t n_atoms;
+    const int64_t* batch_ptr;
+    int64_t batch;
+    const PrepareStructure<T>* structures;
+    int32_t* atom_struct;
+    int32_t* wraps;
+    void* wrapped;  // vec4_t<T> [N]
+    Reduction<T>* reductions;
+    uint32_t* status;
+};
+
+template <typename T>
+struct BinArgs {
+    const StructurePlan<T>* plans;
+    const int64_t* cell_prefix;  // [n_cell + 1] atom prefix over cell-mode structures
+    const int32_t* cell_structs; // [n_cell]
+    int32_t n_cell;
+    int64_t n_cell_atoms;
+    const int32_t* wraps;
+    const void* wrapped;         // vec4_t<T>
+    unsigned long long* bin_counts;  // histogram target / scatter cursors
+    void* ghost_pos;             // vec4_t<T> [G]   (scatter only)
+    int4* ghost_meta;            // [G]             (scatter only)
+    int32_t* self_slot;          // [N]             (scatter only)
+    int32_t* source_list;        // [sources]       (scatter only)
+    uint32_t* status;
+};
+
+template <typename T>
+struct SearchArgs {
+    const T* positions;
+    const int32_t* atom_struct;
+    const int32_t* wraps;
+    const void* wrapped;  // vec4_t<T>
+    const StructurePlan<T>* plans;
+    // cell mode
+    const unsigned long long* bin_start;
+    const void* ghost_pos;  // vec4_t<T>
+    const int4* ghost_meta;
+    const int32_t* self_slot;
+    const int32_t* source_list;
+    int64_t n_sources;
+    // brute mode
+    const int64_t* brute_prefix;  // [n_brute + 1]
+    const int32_t* brute_structs; // [n_brute]
+    int32_t n_brute;
+    int64_t n_brute_atoms;
+    // passes
+    uint32_t* counts;           // count pass output
+    const int64_t* pair_start;  // write pass input
+    int64_t* out_i;
+    int64_t* out_j;
+    int64_t* out_P;
+    int32_t* out_S;
+    T* out_d;
+    T* out_D;
+    int64_t index_offset;
+    uint32_t* status;
+    int32_t half_list;
+    int32_t include_self;
+};
+
+template <typename T>
+void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream);
+
+template <typename T>
+void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream);
+
+template <typename T>
+void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stream);
+
+template <typename T>
+void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t stream);
+
+// Exclusive scans (n+1 outputs).  `tile_words` is workspace of
+// scan_workspace_bytes(n) bytes; it is cleared inside.
+size_t scan_workspace_bytes(int64_t n);
+void launch_scan_u64(const unsigned long long* in, int64_t n, unsigned long long* out,
+                     unsigned long long* out2, void* workspace, uint32_t* status,
+                     cudaStream_t stream);
+void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* workspace,
+                        uint32_t* status, cudaStream_t stream);
+
+}  // namespace tnr
