@@ -8,9 +8,8 @@
 #include "tnr_geometry.h"
 
 #include <algorithm>
-#include <atomic>
 #include <cmath>
-#include <exception>
+#include <string>
 #include <limits>
 #include <mutex>
 #include <thread>
@@ -144,7 +143,7 @@ PeriodicGeometry build_geometry(const double* cells, const uint8_t* pbc,
     // keeping the lowest failing structure and interleaving the batched image
     // limit check at its position.
     int64_t failed_at = batch;
-    std::exception_ptr failure;
+    std::string failure;
     std::mutex guard;
     auto run = [&](int64_t begin, int64_t end) {
         for (int64_t b = begin; b < end; ++b) {
@@ -152,11 +151,11 @@ PeriodicGeometry build_geometry(const double* cells, const uint8_t* pbc,
                 images[b] = structure_geometry(cells + 9 * b, pbc + 3 * b, atom_counts[b],
                                                cutoff, geometry.duals.data() + 9 * b,
                                                geometry.repeats.data() + 3 * b);
-            } catch (...) {
+            } catch (const InputError& error) {
                 std::lock_guard<std::mutex> lock(guard);
                 if (b < failed_at) {
                     failed_at = b;
-                    failure = std::current_exception();
+                    failure = error.what();
                 }
                 return;
             }
@@ -178,7 +177,7 @@ PeriodicGeometry build_geometry(const double* cells, const uint8_t* pbc,
     }
     geometry.image_begin.assign(static_cast<size_t>(batch + 1), 0);
     for (int64_t b = 0; b < batch; ++b) {
-        if (b == failed_at) std::rethrow_exception(failure);
+        if (b == failed_at) throw InputError(failure);
         require_input(geometry.image_begin[b] <= kImageLimit - images[b],
                       "batched periodic image count exceeds the 2^24 resource limit");
         geometry.image_begin[b + 1] = geometry.image_begin[b] + images[b];
