@@ -27,7 +27,7 @@ CORE_LIBRARY = LIB / "libtonari_b200.so"
 TORCH_LIBRARY = LIB / "libtonari_b200_torch.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_SOURCES = ["tnr_kernels.cu"]
+CUDA_SOURCES = ["tnr_kernels.cu", "tnr_static.cu"]
 HOST_SOURCES = ["tnr_api.cpp", "tnr_geometry.cpp"]
 
 
