@@ -392,7 +392,9 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     const size_t prepare_bytes = static_cast<size_t>(batch) *
         (sizeof(PrepareStructure<T>) + sizeof(Reduction<T>)) + 1024;
     const size_t plan_bytes = static_cast<size_t>(batch) *
-        (sizeof(StructurePlan<T>) + 2 * sizeof(int64_t) + 2 * sizeof(int32_t)) + 4096;
+        (sizeof(StructurePlan<T>) + 3 * sizeof(int64_t) + 2 * sizeof(int32_t)) +
+        static_cast<size_t>(geometry.image_begin[batch] + 1) * (sizeof(int4) + sizeof(V4)) +
+        8192;
     const size_t read_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>) + 1024;
     char* pinned = g_pinned.reserve(prepare_bytes + plan_bytes + read_bytes);
     char* pinned_prepare = pinned;
@@ -523,12 +525,49 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     const int64_t n_cell_atoms = cell_prefix.back();
     const int64_t n_brute_atoms = brute_prefix.back();
+    std::vector<int64_t> cell_bin_prefix;
+    for (int32_t b : cell_structs) cell_bin_prefix.push_back(plans[b].bin_begin);
+    cell_bin_prefix.push_back(total_bins);
+    // Image tables: integer shifts enumerated x-major, then y, then z (the
+    // reference's order, tonari csrc/core/geometry.cpp:229-237), and their
+    // Cartesian translations evaluated once in T.
+    const int64_t total_images = geometry.image_begin[batch];
+    std::vector<int4> image_shift(static_cast<size_t>(std::max<int64_t>(total_images, 1)));
+    std::vector<V4> image_translation(image_shift.size());
+    for (int64_t b = 0; b < batch; ++b) {
+        const int32_t* r = geometry.repeats.data() + 3 * b;
+        const T* cell = cell_t.data() + 9 * b;
+        int64_t k = geometry.image_begin[b];
+        if (geometry.image_begin[b + 1] == k) continue;
+        for (int32_t x = -r[0]; x <= r[0]; ++x) {
+            for (int32_t y = -r[1]; y <= r[1]; ++y) {
+                for (int32_t z = -r[2]; z <= r[2]; ++z, ++k) {
+                    image_shift[k] = make_int4(x, y, z, 0);
+                    T t[3];
+                    for (int c = 0; c < 3; ++c) {
+                        volatile T value = T(0);  // evaluated in T, one rounding per operation
+                        value = value + static_cast<T>(x) * cell[c];
+                        value = value + static_cast<T>(y) * cell[3 + c];
+                        value = value + static_cast<T>(z) * cell[6 + c];
+                        t[c] = value;
+                    }
+                    image_translation[k].x = t[0];
+                    image_translation[k].y = t[1];
+                    image_translation[k].z = t[2];
+                    image_translation[k].w = T(0);
+                }
+            }
+        }
+    }
     Upload second;
     const size_t off_plans = second.add(plans.data(), plans.size());
+    const size_t off_image_shift = second.add(image_shift.data(), image_shift.size());
+    const size_t off_image_translation = second.add(image_translation.data(), image_translation.size());
     const size_t off_cell_prefix = second.add(cell_prefix.data(), cell_prefix.size());
     const size_t off_cell_structs = second.add(cell_structs.data(), cell_structs.size());
     const size_t off_brute_prefix = second.add(brute_prefix.data(), brute_prefix.size());
     const size_t off_brute_structs = second.add(brute_structs.data(), brute_structs.size());
+    const size_t off_cell_bins = second.add(cell_bin_prefix.data(), cell_bin_prefix.size());
     char* second_device = second.commit(workspace, stream, pinned_plan);
     auto* d_plans = reinterpret_cast<StructurePlan<T>*>(second_device + off_plans);
 
@@ -538,6 +577,8 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     int4* d_ghost_meta = nullptr;
     int32_t* d_self_slot = nullptr;
     int32_t* d_source_list = nullptr;
+    uint32_t* d_mask_words = nullptr;
+    unsigned long long* d_bin_word_start = nullptr;
     const int64_t scan_items = std::max<int64_t>(n_atoms, total_bins);
     void* d_scan_workspace = workspace.raw(scan_workspace_bytes(scan_items));
     BinArgs<T> bin_args{};
@@ -549,6 +590,8 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     bin_args.wraps = d_wraps;
     bin_args.wrapped = d_wrapped;
     bin_args.status = d_status;
+    bin_args.image_shift = reinterpret_cast<const int4*>(second_device + off_image_shift);
+    bin_args.image_translation = second_device + off_image_translation;
     if (n_cell_atoms > 0) {
         auto* d_bin_counts = workspace.get<unsigned long long>(total_bins);
         d_bin_start = workspace.get<unsigned long long>(total_bins + 1);
@@ -561,11 +604,32 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         launch_scan_u64(d_bin_counts, total_bins, d_bin_start, d_cursor, d_scan_workspace, d_status,
                         stream);
         check_launch("bin scan kernel");
-        unsigned long long packed_total = 0;
+        // Bitmask words for the count pass -> write pass hand-off: per-bin
+        // word counts, scanned into per-bin offsets.
+        SearchArgs<T> words_args{};
+        words_args.plans = d_plans;
+        words_args.bin_start = d_bin_start;
+        words_args.cell_bin_prefix = reinterpret_cast<const int64_t*>(second_device + off_cell_bins);
+        words_args.cell_structs = bin_args.cell_structs;
+        words_args.n_cell = bin_args.n_cell;
+        words_args.n_bins = total_bins;
+        auto* d_bin_words = workspace.get<unsigned long long>(total_bins);
+        d_bin_word_start = workspace.get<unsigned long long>(total_bins + 1);
+        launch_stencil_words(words_args, d_bin_words, stream);
+        check_launch("stencil words kernel");
+        launch_scan_u64(d_bin_words, total_bins, d_bin_word_start, nullptr, d_scan_workspace,
+                        d_status, stream);
+        check_launch("mask scan kernel");
+        unsigned long long packed_total = 0, mask_words = 0;
         check_cuda(cudaMemcpyAsync(pinned_read, d_bin_start + total_bins, sizeof(packed_total),
                                    cudaMemcpyDeviceToHost, stream), "read ghost total");
+        check_cuda(cudaMemcpyAsync(pinned_read + 8, d_bin_word_start + total_bins, sizeof(mask_words),
+                                   cudaMemcpyDeviceToHost, stream), "read mask words");
         check_cuda(cudaStreamSynchronize(stream), "ghost total");
         std::memcpy(&packed_total, pinned_read, sizeof(packed_total));
+        std::memcpy(&mask_words, pinned_read + 8, sizeof(mask_words));
+        require_search(mask_words < (1ull << 32), "cell-list candidate bitmask exceeds uint32 indexing");
+        d_mask_words = workspace.get<uint32_t>(mask_words);
         const int64_t ghosts = static_cast<int64_t>(packed_total & 0xffffffffull);
         const int64_t sources = static_cast<int64_t>(packed_total >> 32);
         require_search(sources == n_cell_atoms && ghosts >= sources &&
@@ -601,6 +665,13 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.self_slot = d_self_slot;
     search.source_list = d_source_list;
     search.n_sources = n_cell_atoms;
+    search.image_shift = bin_args.image_shift;
+    search.mask_words = d_mask_words;
+    search.bin_word_start = d_bin_word_start;
+    search.cell_bin_prefix = reinterpret_cast<const int64_t*>(second_device + off_cell_bins);
+    search.cell_structs = reinterpret_cast<const int32_t*>(second_device + off_cell_structs);
+    search.n_cell = static_cast<int32_t>(cell_structs.size());
+    search.n_bins = total_bins;
     search.brute_prefix = reinterpret_cast<const int64_t*>(second_device + off_brute_prefix);
     search.brute_structs = reinterpret_cast<const int32_t*>(second_device + off_brute_structs);
     search.n_brute = static_cast<int32_t>(brute_structs.size());

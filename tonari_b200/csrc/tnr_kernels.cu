@@ -249,23 +249,16 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
     const int32_t wrap[3] = {args.wraps[3 * atom], args.wraps[3 * atom + 1],
                              args.wraps[3 * atom + 2]};
     const int32_t center = (plan.n_images - 1) / 2;
+    const V* translations = reinterpret_cast<const V*>(args.image_translation) + plan.image_begin;
     for (int32_t k = 0; k < plan.n_images; ++k) {
-        int32_t image[3];
-        decode_image(k, plan.repeats, image);
+        const V tr = translations[k];
         T g[3];
-        bool inside = true;
-#pragma unroll
-        for (int axis = 0; axis < 3; ++axis) {
-            T translation = T(0);
-#pragma unroll
-            for (int a = 0; a < 3; ++a) {
-                translation = add_rn(translation,
-                                     mul_rn(static_cast<T>(image[a]), plan.cell[3 * a + axis]));
-            }
-            const T base = axis == 0 ? q.x : (axis == 1 ? q.y : q.z);
-            g[axis] = add_rn(base, translation);
-            inside = inside && g[axis] >= plan.lower[axis] && g[axis] <= plan.upper[axis];
-        }
+        g[0] = add_rn(q.x, tr.x);
+        g[1] = add_rn(q.y, tr.y);
+        g[2] = add_rn(q.z, tr.z);
+        const bool inside = g[0] >= plan.lower[0] && g[0] <= plan.upper[0] &&
+                            g[1] >= plan.lower[1] && g[1] <= plan.upper[1] &&
+                            g[2] >= plan.lower[2] && g[2] <= plan.upper[2];
         if (!inside && k != center) continue;
         const int32_t bx = bin_axis(g[0], plan.origin[0], plan.inv_edge, plan.dims[0]);
         const int32_t by = bin_axis(g[1], plan.origin[1], plan.inv_edge, plan.dims[1]);
@@ -283,8 +276,9 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
             record.z = g[2];
             record.w = index_to_lane(static_cast<int32_t>(atom), T(0));
             reinterpret_cast<V*>(args.ghost_pos)[slot] = record;
-            args.ghost_meta[slot] = make_int4(image[0] - wrap[0], image[1] - wrap[1],
-                                              image[2] - wrap[2], static_cast<int32_t>(atom));
+            const int4 image = args.image_shift[plan.image_begin + k];
+            args.ghost_meta[slot] = make_int4(image.x - wrap[0], image.y - wrap[1],
+                                              image.z - wrap[2], static_cast<int32_t>(atom));
             if (k == center) {
                 args.source_list[static_cast<uint32_t>(old >> 32)] = static_cast<int32_t>(atom);
                 args.self_slot[atom] = static_cast<int32_t>(slot);
@@ -334,34 +328,43 @@ __device__ __forceinline__ void exact_displacement(const T* __restrict__ positio
     }
 }
 
-__device__ __forceinline__ bool shift_fits_int32(const long long (&shift)[3]) {
-    return shift[0] >= INT_MIN && shift[0] <= INT_MAX && shift[1] >= INT_MIN &&
-           shift[1] <= INT_MAX && shift[2] >= INT_MIN && shift[2] <= INT_MAX;
+
+// ---- cell list -------------------------------------------------------------
+//
+// One warp per bin: the bin's 27-bin stencil is loaded once (nine z-rows,
+// each a contiguous slot range of the cell-sorted ghost array) and the warp
+// then serves every source atom of the bin in turn.  For one source the warp
+// walks the concatenated rows 32 candidates per iteration; each lane keeps
+// its own (row, slot) cursor and advances it by 32, and the next iteration's
+// record is loaded before the current one is evaluated so that two loads are
+// in flight per lane.  Candidate k of a source is lane k % 32 of iteration
+// k / 32 in both passes, so the count pass hands its per-iteration ballots to
+// the write pass as a bitmask at a deterministic offset:
+//   bin_word_start[bin] + (source rank in bin) * ceil(candidates / 32).
+
+struct StencilRows {
+    int32_t prefix[16];  // candidate index where row r starts; [9] = total; [10..] = INT_MAX
+    int32_t delta[9];    // slot = candidate index + delta[row]
+};
+
+template <typename T>
+__device__ __forceinline__ void bin_coordinates(const StructurePlan<T>& plan, int64_t bin,
+                                                int32_t& bx, int32_t& by, int32_t& bz) {
+    const int64_t local = bin - plan.bin_begin;
+    bz = static_cast<int32_t>(local % plan.dims[2]);
+    by = static_cast<int32_t>((local / plan.dims[2]) % plan.dims[1]);
+    bx = static_cast<int32_t>(local / (static_cast<int64_t>(plan.dims[2]) * plan.dims[1]));
 }
 
-// Cell list: one warp per source atom (sources in cell-sorted order, so
-// neighbouring warps share stencil bins in L1).  The 27-bin stencil is nine
-// z-rows, each a contiguous slot range of the cell-sorted ghost array; the
-// warp walks their concatenation 32 candidates at a time so lanes stay busy
-// across row boundaries.
-template <typename T, bool Write>
-__global__ void __launch_bounds__(kSearchThreads) cell_search_kernel(SearchArgs<T> args) {
-    using V = vec4_t<T>;
-    __shared__ int64_t row_begin[kSearchWarps][9];
-    __shared__ int64_t row_prefix[kSearchWarps][10];
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int64_t work = static_cast<int64_t>(blockIdx.x) * kSearchWarps + warp;
-    if (work >= args.n_sources) return;
-
-    const int32_t source = args.source_list[work];
-    const StructurePlan<T>& plan = args.plans[args.atom_struct[source]];
-    const V qs = reinterpret_cast<const V*>(args.wrapped)[source];
-    const int32_t bx = bin_axis(qs.x, plan.origin[0], plan.inv_edge, plan.dims[0]);
-    const int32_t by = bin_axis(qs.y, plan.origin[1], plan.inv_edge, plan.dims[1]);
-    const int32_t bz = bin_axis(qs.z, plan.origin[2], plan.inv_edge, plan.dims[2]);
-
-    int64_t begin = 0, length = 0;
+// Lanes 0-8 fetch the slot range of one stencil row each and the warp builds
+// the row prefix table (into `rows` when non-null); returns the total
+// candidate count (warp-uniform).
+template <typename T>
+__device__ __forceinline__ int32_t load_stencil(const StructurePlan<T>& plan,
+                                                const unsigned long long* __restrict__ bin_start,
+                                                int32_t bx, int32_t by, int32_t bz,
+                                                StencilRows* rows, int lane) {
+    int32_t begin = 0, length = 0;
     if (lane < 9) {
         const int32_t x = bx + lane / 3 - 1;
         const int32_t y = by + lane % 3 - 1;
@@ -370,170 +373,485 @@ __global__ void __launch_bounds__(kSearchThreads) cell_search_kernel(SearchArgs<
             const int32_t z1 = min(bz + 1, plan.dims[2] - 1);
             const int64_t row = plan.bin_begin +
                 (static_cast<int64_t>(x) * plan.dims[1] + y) * plan.dims[2];
-            begin = static_cast<int64_t>(args.bin_start[row + z0] & 0xffffffffull);
-            const int64_t end = static_cast<int64_t>(args.bin_start[row + z1 + 1] & 0xffffffffull);
-            length = end - begin;
+            begin = static_cast<int32_t>(bin_start[row + z0] & 0xffffffffull);
+            length = static_cast<int32_t>(bin_start[row + z1 + 1] & 0xffffffffull) - begin;
         }
     }
-    const int64_t inclusive = warp_inclusive_sum(length);
-    if (lane < 9) {
-        row_begin[warp][lane] = begin;
-        row_prefix[warp][lane + 1] = inclusive;
+    int32_t inclusive = length;
+#pragma unroll
+    for (int offset = 1; offset < 16; offset <<= 1) {
+        const int32_t other = __shfl_up_sync(kFullMask, inclusive, offset);
+        if (lane >= offset) inclusive += other;
     }
-    if (lane == 0) row_prefix[warp][0] = 0;
+    const int32_t total = __shfl_sync(kFullMask, inclusive, 8);
+    if (rows) {
+        if (lane < 9) {
+            rows->prefix[lane] = inclusive - length;
+            rows->delta[lane] = begin - (inclusive - length);
+        } else if (lane == 9) {
+            rows->prefix[9] = total;
+        } else if (lane < 16) {
+            rows->prefix[lane] = INT_MAX;
+        }
+    }
     __syncwarp();
-    const int64_t total = __shfl_sync(kFullMask, inclusive, 8);
+    return total;
+}
 
-    const int32_t self = args.self_slot[source];
-    const long long ws[3] = {args.wraps[3 * source], args.wraps[3 * source + 1],
-                             args.wraps[3 * source + 2]};
-    const bool half = args.half_list != 0;
-    const bool include_self = args.include_self != 0;
-    const bool need_vector = args.out_d != nullptr || args.out_D != nullptr;
-    int64_t out_base = 0;
-    if constexpr (Write) out_base = args.pair_start[source];
-    uint32_t count = 0;
-    int row = 0;
-    for (int64_t base = 0; base < total; base += 32) {
-        const int64_t k = base + lane;
-        bool accept = false;
-        int32_t target = -1;
-        long long shift[3] = {0, 0, 0};
-        bool shift_known = false;
-        T vec[3] = {T(0), T(0), T(0)};
-        bool vec_known = false;
-        if (k < total) {
-            while (k >= row_prefix[warp][row + 1]) ++row;
-            const int64_t slot = row_begin[warp][row] + (k - row_prefix[warp][row]);
-            const V g = reinterpret_cast<const V*>(args.ghost_pos)[slot];
-            const T dx = g.x - qs.x;
-            const T dy = g.y - qs.y;
-            const T dz = g.z - qs.z;
-            const T d2 = dx * dx + dy * dy + dz * dz;
-            if (d2 < plan.search_squared) {
-                target = lane_to_index(g.w);
-                if (slot == self) {
-                    accept = include_self;  // the zero-shift self pair
-                    shift_known = true;
-                    vec_known = true;
+// Slot of candidate index k (0 <= k < total): the last row whose prefix is
+// <= k, found in four fixed steps.
+__device__ __forceinline__ int32_t slot_of(const StencilRows& rows, int32_t k) {
+    int32_t r = 0;
+    r += (rows.prefix[r + 8] <= k) ? 8 : 0;
+    r += (rows.prefix[r + 4] <= k) ? 4 : 0;
+    r += (rows.prefix[r + 2] <= k) ? 2 : 0;
+    r += (rows.prefix[r + 1] <= k) ? 1 : 0;
+    return k + rows.delta[r];
+}
+
+// Exact decision for the rare candidates (band shell, periodic self images in
+// half mode, the zero-shift self pair).
+template <typename T>
+__device__ __forceinline__ bool rare_decision(const SearchArgs<T>& args,
+                                              const StructurePlan<T>& plan, int32_t source,
+                                              int32_t slot, int32_t self, int32_t target,
+                                              bool exact, const long long (&ws)[3]) {
+    if (slot == self) return args.include_self != 0;
+    if (args.half_list && target < source) return false;
+    const int4 meta = args.ghost_meta[slot];
+    const long long shift[3] = {meta.x + ws[0], meta.y + ws[1], meta.z + ws[2]};
+    if (args.half_list && target == source && !canonical_shift(shift)) return false;
+    if (!exact) return true;
+    T vec[3];
+    exact_displacement(args.positions, source, target, shift, plan.cell, vec);
+    return exact_norm2(vec[0], vec[1], vec[2]) < plan.cutoff_squared;
+}
+
+// Per bin: bitmask words of all its sources (sources * ceil(candidates / 32)).
+template <typename T>
+__global__ void __launch_bounds__(kBinThreads) stencil_words_kernel(SearchArgs<T> args,
+                                                                    int64_t n_bins,
+                                                                    unsigned long long* bin_words) {
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t bin = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         bin < n_bins; bin += stride) {
+        const unsigned long long sources =
+            (args.bin_start[bin + 1] >> 32) - (args.bin_start[bin] >> 32);
+        if (sources == 0) {
+            if (lane == 0) bin_words[bin] = 0;
+            continue;
+        }
+        const int32_t c = segment_of(args.cell_bin_prefix, args.n_cell, bin);
+        const StructurePlan<T>& plan = args.plans[args.cell_structs[c]];
+        int32_t bx, by, bz;
+        bin_coordinates(plan, bin, bx, by, bz);
+        const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz,
+                                           static_cast<StencilRows*>(nullptr), lane);
+        if (lane == 0) bin_words[bin] = sources * static_cast<unsigned long long>((total + 31) >> 5);
+    }
+}
+
+// Count pass, lanes = sources: the warp serves up to 32 source atoms of its
+// bin at once.  Per 32-candidate chunk every lane loads one candidate record
+// into shared memory; each record is then read back as a broadcast and
+// tested against all lanes' sources, so one short instruction sequence
+// evaluates 32 source-candidate pairs.  Candidates in the band shell, the
+// zero-shift self pair and (half list) periodic self images are flagged in a
+// per-lane bit word and decided after the chunk.  Accepted-candidate bits are
+// stored transposed -- word w of source rank r at base + w * S + r, S the
+// bin's source count -- so each chunk's store is coalesced.
+template <typename T, bool Half>
+__global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T> args) {
+    using V = vec4_t<T>;
+    __shared__ StencilRows stencil[kSearchWarps];
+    __shared__ V tile[kSearchWarps][32];
+    __shared__ int32_t tile_slot[kSearchWarps][32];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t bin = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         bin < args.n_bins; bin += stride) {
+        const uint32_t first_source = static_cast<uint32_t>(args.bin_start[bin] >> 32);
+        const uint32_t n_sources = static_cast<uint32_t>(args.bin_start[bin + 1] >> 32) - first_source;
+        if (n_sources == 0) continue;
+        const int32_t c = segment_of(args.cell_bin_prefix, args.n_cell, bin);
+        const StructurePlan<T>& plan = args.plans[args.cell_structs[c]];
+        int32_t bx, by, bz;
+        bin_coordinates(plan, bin, bx, by, bz);
+        StencilRows& rows = stencil[warp];
+        const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz, &rows, lane);
+        const int32_t words = (total + 31) >> 5;
+        uint32_t* mask = args.mask_words + args.bin_word_start[bin];
+        const T search2 = plan.search_squared;
+        const T inner2 = plan.inner_squared;
+        V* my_tile = tile[warp];
+        int32_t* my_slot = tile_slot[warp];
+
+        // Lane groups: with S <= 16 sources the warp splits into G = 32 / P groups
+        // of P lanes (P = next power of two >= S); group g tests candidates
+        // j = g, g + G, ... of each chunk against its P sources, and the groups'
+        // bits are OR-combined afterwards.
+        const uint32_t width = n_sources >= 32 ? 32u : (n_sources <= 1 ? 1u : 1u << (32 - __clz(n_sources - 1)));
+        const int groups = 32 / static_cast<int>(width);
+        const int my_group = lane / static_cast<int>(width);
+        const uint32_t my_rank = static_cast<uint32_t>(lane) % width;
+
+        for (uint32_t base = 0; base < n_sources; base += width) {
+            const uint32_t rank = base + my_rank;
+            const bool active = rank < n_sources;
+            int32_t source = -1;
+            // Idle lanes test against a NaN position: no candidate is ever inner
+            // or rare for them, so they never reach the exact test.
+            V qs;
+            qs.x = qs.y = qs.z = qs.w = static_cast<T>(NAN);
+            int32_t self = -1;
+            long long ws[3] = {0, 0, 0};
+            if (active) {
+                source = args.source_list[first_source + rank];
+                qs = reinterpret_cast<const V*>(args.wrapped)[source];
+                self = args.self_slot[source];
+                ws[0] = args.wraps[3 * source];
+                ws[1] = args.wraps[3 * source + 1];
+                ws[2] = args.wraps[3 * source + 2];
+            }
+            uint32_t count = 0;
+            for (int32_t w = 0; w < words; ++w) {
+                V record;
+                int32_t record_slot = -1;
+                const int32_t k = 32 * w + lane;
+                if (k < total) {
+                    const int32_t slot = slot_of(rows, k);
+                    record = reinterpret_cast<const V*>(args.ghost_pos)[slot];
+                    record_slot = slot;
                 } else {
-                    bool identity = true;
-                    if (half && target != source) identity = source < target;
-                    const bool exact = !(d2 < plan.inner_squared);
-                    if ((half && target == source) || exact || (Write && (args.out_S || need_vector))) {
-                        const int4 meta = args.ghost_meta[slot];
-                        shift[0] = static_cast<long long>(meta.x) + ws[0];
-                        shift[1] = static_cast<long long>(meta.y) + ws[1];
-                        shift[2] = static_cast<long long>(meta.z) + ws[2];
-                        shift_known = true;
-                        if (half && target == source) identity = canonical_shift(shift);
+                    record.x = static_cast<T>(INFINITY);
+                    record.y = T(0);
+                    record.z = T(0);
+                    record.w = index_to_lane(-1, T(0));
+                }
+                __syncwarp();
+                my_tile[lane] = record;
+                my_slot[lane] = record_slot;
+                __syncwarp();
+                uint32_t bits = 0;
+                uint32_t rare_bits = 0;
+    #pragma unroll 4
+                for (int j = my_group; j < 32; j += groups) {
+                    const V g = my_tile[j];
+                    const T dx = g.x - qs.x;
+                    const T dy = g.y - qs.y;
+                    const T dz = g.z - qs.z;
+                    const T d2 = dx * dx + dy * dy + dz * dz;
+                    const bool inner = d2 < inner2;
+                    const int32_t target = lane_to_index(g.w);
+                    bool cheap = inner;
+                    bool rare = !inner && d2 < search2;
+                    if constexpr (Half) {
+                        cheap = cheap && target > source;
+                        rare = rare || (inner && target == source);
+                    } else {
+                        // Full list: inner candidates with target == source (the
+                        // zero-shift self pair, periodic self images) are decided
+                        // exactly below.
+                        cheap = cheap && target != source;
+                        rare = rare || (inner && target == source);
                     }
-                    if (identity) {
-                        if (exact || (Write && need_vector)) {
-                            exact_displacement(args.positions, source, target, shift, plan.cell, vec);
-                            vec_known = true;
-                            accept = !exact ||
-                                exact_norm2(vec[0], vec[1], vec[2]) < plan.cutoff_squared;
-                        } else {
-                            accept = true;
-                        }
+                    bits |= static_cast<uint32_t>(cheap) << j;
+                    rare_bits |= static_cast<uint32_t>(rare) << j;
+                }
+                if (!active) rare_bits = 0;
+                while (rare_bits) {
+                    const int j = __ffs(rare_bits) - 1;
+                    rare_bits &= rare_bits - 1;
+                    const V g = my_tile[j];
+                    const T dx = g.x - qs.x;
+                    const T dy = g.y - qs.y;
+                    const T dz = g.z - qs.z;
+                    const bool exact = !((dx * dx + dy * dy + dz * dz) < inner2);
+                    if (rare_decision(args, plan, source, my_slot[j], self, lane_to_index(g.w),
+                                      exact, ws)) {
+                        bits |= 1u << j;
                     }
                 }
+                for (int offset = static_cast<int>(width); offset < 32; offset <<= 1) {
+                    bits |= __shfl_xor_sync(kFullMask, bits, offset);
+                }
+                if (!active) bits = 0;
+                if (active && my_group == 0) mask[static_cast<int64_t>(w) * n_sources + rank] = bits;
+                count += __popc(bits);
             }
-        }
-        (void)shift_known;
-        (void)vec_known;
-        const unsigned mask = __ballot_sync(kFullMask, accept);
-        if constexpr (Write) {
-            if (accept) {
-                const int64_t o = out_base + count + __popc(mask & ((1u << lane) - 1u));
-                emit_pair(args, o, source, target, shift, vec);
-            }
-        }
-        count += __popc(mask);
-    }
-    if constexpr (!Write) {
-        if (lane == 0) {
-            args.counts[source] = count;
-            if (count > static_cast<uint32_t>(INT_MAX)) {
-                atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
+            if (active && my_group == 0) {
+                args.counts[source] = count;
+                if (count > static_cast<uint32_t>(INT_MAX)) {
+                    atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
+                }
             }
         }
     }
 }
 
-// Brute force: one warp per source atom of a brute-force structure; lanes
-// stride over the N x I (target, image) candidates, target fastest so that
-// consecutive lanes read consecutive atoms.  Every candidate takes the exact
-// predicate (tonari csrc/core/neighbors_cpu.cpp:222-273).
-template <typename T, bool Write>
-__global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs<T> args) {
+// Write pass: replays the candidate walk, reading the count pass's ballots
+// instead of recomputing distances, and queues accepted slots in shared
+// memory; every 32 queued pairs are emitted by the whole warp at once
+// (record loads, exact displacement, 32 consecutive output rows).
+template <typename T>
+__device__ __forceinline__ void emit_queued(const SearchArgs<T>& args, const StructurePlan<T>& plan,
+                                            int32_t source, const long long (&ws)[3],
+                                            int32_t slot, int64_t row_out, bool active,
+                                            bool need_shift, bool need_vector) {
+    if (!active) return;
+    const int4 meta = args.ghost_meta[slot];
+    const int32_t target = meta.w;
+    long long shift[3] = {0, 0, 0};
+    if (need_shift) {
+        shift[0] = meta.x + ws[0];
+        shift[1] = meta.y + ws[1];
+        shift[2] = meta.z + ws[2];
+    }
+    T vec[3] = {T(0), T(0), T(0)};
+    if (need_vector) exact_displacement(args.positions, source, target, shift, plan.cell, vec);
+    emit_pair(args, row_out, source, target, shift, vec);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T> args) {
+    __shared__ StencilRows stencil[kSearchWarps];
+    __shared__ int32_t queue[kSearchWarps][64];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int64_t work = static_cast<int64_t>(blockIdx.x) * kSearchWarps + warp;
-    if (work >= args.n_brute_atoms) return;
-    const int32_t c = segment_of(args.brute_prefix, args.n_brute, work);
-    const StructurePlan<T>& plan = args.plans[args.brute_structs[c]];
-    const int64_t source = plan.atom_begin + (work - args.brute_prefix[c]);
-    const long long ws[3] = {args.wraps[3 * source], args.wraps[3 * source + 1],
-                             args.wraps[3 * source + 2]};
-    const bool half = args.half_list != 0;
-    const bool include_self = args.include_self != 0;
-    const int64_t n = plan.n_atoms;
-    const int64_t total = n * plan.n_images;
-    int64_t out_base = 0;
-    if constexpr (Write) out_base = args.pair_start[source];
-    uint32_t count = 0;
-    for (int64_t base = 0; base < total; base += 32) {
-        const int64_t k = base + lane;
-        bool accept = false;
-        int64_t target = 0;
-        long long shift[3] = {0, 0, 0};
-        T vec[3] = {T(0), T(0), T(0)};
-        if (k < total) {
-            const int64_t image_index = k / n;
-            target = plan.atom_begin + (k - image_index * n);
-            int32_t image[3];
-            decode_image(static_cast<int32_t>(image_index), plan.repeats, image);
-#pragma unroll
-            for (int a = 0; a < 3; ++a) {
-                shift[a] = static_cast<long long>(image[a]) -
-                           static_cast<long long>(args.wraps[3 * target + a]) + ws[a];
+    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t bin = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         bin < args.n_bins; bin += stride) {
+        const uint32_t first_source = static_cast<uint32_t>(args.bin_start[bin] >> 32);
+        const uint32_t last_source = static_cast<uint32_t>(args.bin_start[bin + 1] >> 32);
+        if (first_source == last_source) continue;
+        const int32_t c = segment_of(args.cell_bin_prefix, args.n_cell, bin);
+        const StructurePlan<T>& plan = args.plans[args.cell_structs[c]];
+        int32_t bx, by, bz;
+        bin_coordinates(plan, bin, bx, by, bz);
+        StencilRows& rows = stencil[warp];
+        const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz, &rows, lane);
+        const int32_t words = (total + 31) >> 5;
+        const unsigned long long word_base = args.bin_word_start[bin];
+        const bool need_vector = args.out_d != nullptr || args.out_D != nullptr;
+        const bool need_shift = need_vector || args.out_S != nullptr;
+        const unsigned below = (1u << lane) - 1u;
+        int32_t* q = queue[warp];
+
+        const uint32_t n_bin_sources = last_source - first_source;
+        for (uint32_t base = 0; base < n_bin_sources; base += 32) {
+            // One lane per source fetches that source's data; the warp then
+            // serves the sources one after another from registers.
+            const uint32_t mine = base + lane;
+            int32_t my_source = 0, my_count = 0;
+            int64_t my_start = 0;
+            int32_t my_wrap[3] = {0, 0, 0};
+            if (mine < n_bin_sources) {
+                my_source = args.source_list[first_source + mine];
+                my_count = static_cast<int32_t>(args.counts[my_source]);
+                my_start = args.pair_start[my_source];
+                my_wrap[0] = args.wraps[3 * my_source];
+                my_wrap[1] = args.wraps[3 * my_source + 1];
+                my_wrap[2] = args.wraps[3 * my_source + 2];
             }
-            if (keep_identity(source, target, shift, half, include_self)) {
-                const bool zero_self =
-                    source == target && shift[0] == 0 && shift[1] == 0 && shift[2] == 0;
-                if (zero_self) {
-                    accept = true;
-                } else {
-                    exact_displacement(args.positions, source, target, shift, plan.cell, vec);
-                    accept = exact_norm2(vec[0], vec[1], vec[2]) < plan.cutoff_squared;
+            const uint32_t batch = min(32u, n_bin_sources - base);
+            for (uint32_t b = 0; b < batch; ++b) {
+                if (__shfl_sync(kFullMask, my_count, b) == 0) continue;
+                const int32_t source = __shfl_sync(kFullMask, my_source, b);
+                int64_t out_row = __shfl_sync(kFullMask, my_start, b);
+                const long long ws[3] = {__shfl_sync(kFullMask, my_wrap[0], b),
+                                         __shfl_sync(kFullMask, my_wrap[1], b),
+                                         __shfl_sync(kFullMask, my_wrap[2], b)};
+                const uint32_t* mask = args.mask_words + word_base + base + b;
+                int32_t queued = 0;
+                for (int32_t chunk = 0; chunk < words; chunk += 32) {
+                    const uint32_t my_word =
+                        chunk + lane < words
+                            ? mask[static_cast<int64_t>(chunk + lane) * n_bin_sources] : 0u;
+                    const int32_t span = min(32, words - chunk);
+                    for (int32_t j = 0; j < span; ++j) {
+                        const uint32_t word = __shfl_sync(kFullMask, my_word, j);
+                        if (word != 0u) {
+                            if ((word >> lane) & 1u) {
+                                q[queued + __popc(word & below)] = 32 * (chunk + j) + lane;
+                            }
+                            queued += __popc(word);
+                            if (queued >= 32) {
+                                __syncwarp();
+                                emit_queued(args, plan, source, ws, slot_of(rows, q[lane]),
+                                            out_row + lane, true, need_shift, need_vector);
+                                __syncwarp();
+                                if (lane < queued - 32) q[lane] = q[32 + lane];
+                                __syncwarp();
+                                queued -= 32;
+                                out_row += 32;
+                            }
+                        }
+                    }
                 }
-                if (accept && !shift_fits_int32(shift)) {
-                    atomicOr(args.status, static_cast<uint32_t>(kStatusShiftRange));
-                }
+                __syncwarp();
+                emit_queued(args, plan, source, ws, lane < queued ? slot_of(rows, q[lane]) : 0,
+                            out_row + lane, lane < queued, need_shift, need_vector);
+                __syncwarp();
             }
         }
-        const unsigned mask = __ballot_sync(kFullMask, accept);
-        if constexpr (Write) {
-            if (accept) {
-                const int64_t o = out_base + count + __popc(mask & ((1u << lane) - 1u));
-                emit_pair(args, o, source, target, shift, vec);
-            }
-        }
-        count += __popc(mask);
     }
-    if constexpr (!Write) {
-        if (lane == 0) {
-            args.counts[source] = count;
-            if (count > static_cast<uint32_t>(INT_MAX)) {
-                atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
+}
+
+// Brute force: one warp per source atom of a brute-force structure (grid-
+// stride over those atoms); lanes stride over the N x I (target, image)
+// candidates, target fastest so that consecutive lanes read consecutive
+// atoms, with (target, image) cursors advanced incrementally.  Every
+// candidate takes the exact predicate (tonari csrc/core/neighbors_cpu.cpp:
+// 222-273).  The write pass queues accepted candidates in shared memory and
+// emits them 32 at a time into consecutive output rows.
+template <typename T>
+struct BruteCandidate {
+    bool accept;
+    long long shift[3];
+    T vec[3];
+};
+
+template <typename T>
+__device__ __forceinline__ BruteCandidate<T> brute_evaluate(const SearchArgs<T>& args,
+                                                            const StructurePlan<T>& plan,
+                                                            int64_t source, int64_t target,
+                                                            int32_t image_index, const T (&ps)[3],
+                                                            const long long (&ws)[3]) {
+    BruteCandidate<T> out;
+    const int4 image = args.image_shift[plan.image_begin + image_index];
+    out.shift[0] = static_cast<long long>(image.x) - args.wraps[3 * target] + ws[0];
+    out.shift[1] = static_cast<long long>(image.y) - args.wraps[3 * target + 1] + ws[1];
+    out.shift[2] = static_cast<long long>(image.z) - args.wraps[3 * target + 2] + ws[2];
+    out.vec[0] = out.vec[1] = out.vec[2] = T(0);
+    out.accept = false;
+    if (!keep_identity(source, target, out.shift, args.half_list != 0, args.include_self != 0)) {
+        return out;
+    }
+    const bool zero_self =
+        source == target && out.shift[0] == 0 && out.shift[1] == 0 && out.shift[2] == 0;
+    if (zero_self) {
+        out.accept = true;
+        return out;
+    }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        out.vec[c] = exact_component(args.positions[3 * target + c], ps[c], out.shift, plan.cell, c);
+    }
+    out.accept = exact_norm2(out.vec[0], out.vec[1], out.vec[2]) < plan.cutoff_squared;
+    return out;
+}
+
+template <typename T, bool Write>
+__global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs<T> args) {
+    __shared__ int2 queue[kSearchWarps][64];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned below = (1u << lane) - 1u;
+    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t work = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         work < args.n_brute_atoms; work += stride) {
+        const int32_t c = segment_of(args.brute_prefix, args.n_brute, work);
+        const StructurePlan<T>& plan = args.plans[args.brute_structs[c]];
+        const int64_t source = plan.atom_begin + (work - args.brute_prefix[c]);
+        if constexpr (Write) {
+            if (args.counts[source] == 0) continue;
+        }
+        const T ps[3] = {args.positions[3 * source], args.positions[3 * source + 1],
+                         args.positions[3 * source + 2]};
+        const long long ws[3] = {args.wraps[3 * source], args.wraps[3 * source + 1],
+                                 args.wraps[3 * source + 2]};
+        const int32_t n = plan.n_atoms;
+        const int32_t images = plan.n_images;
+        const int32_t step_images = 32 / n;
+        const int32_t step_atoms = 32 % n;
+        int32_t t = lane % n;
+        int32_t image = lane / n;
+        uint32_t count = 0;
+        int64_t out_row = 0;
+        int32_t queued = 0;
+        if constexpr (Write) out_row = args.pair_start[source];
+        // Warp-uniform trip count: ceil(n * images / 32) iterations.
+        const int64_t trips = (static_cast<int64_t>(n) * images + 31) / 32;
+        for (int64_t trip = 0; trip < trips; ++trip) {
+            bool accept = false;
+            if (image < images) {
+                const BruteCandidate<T> cand =
+                    brute_evaluate(args, plan, source, plan.atom_begin + t, image, ps, ws);
+                accept = cand.accept;
+                if (!Write && accept) {
+                    if (cand.shift[0] < INT_MIN || cand.shift[0] > INT_MAX ||
+                        cand.shift[1] < INT_MIN || cand.shift[1] > INT_MAX ||
+                        cand.shift[2] < INT_MIN || cand.shift[2] > INT_MAX) {
+                        atomicOr(args.status, static_cast<uint32_t>(kStatusShiftRange));
+                    }
+                }
+            }
+            const unsigned ballot = __ballot_sync(kFullMask, accept);
+            if constexpr (Write) {
+                if (ballot) {
+                    int2* q = queue[warp];
+                    if (accept) q[queued + __popc(ballot & below)] = make_int2(t, image);
+                    queued += __popc(ballot);
+                    if (queued >= 32) {
+                        __syncwarp();
+                        const int2 item = q[lane];
+                        const BruteCandidate<T> cand = brute_evaluate(
+                            args, plan, source, plan.atom_begin + item.x, item.y, ps, ws);
+                        emit_pair(args, out_row + lane, source, plan.atom_begin + item.x,
+                                  cand.shift, cand.vec);
+                        __syncwarp();
+                        if (lane < queued - 32) q[lane] = q[32 + lane];
+                        __syncwarp();
+                        queued -= 32;
+                        out_row += 32;
+                    }
+                }
+            } else {
+                count += __popc(ballot);
+            }
+            t += step_atoms;
+            image += step_images;
+            if (t >= n) {
+                t -= n;
+                ++image;
+            }
+        }
+        if constexpr (Write) {
+            __syncwarp();
+            if (lane < queued) {
+                const int2 item = queue[warp][lane];
+                const BruteCandidate<T> cand = brute_evaluate(
+                    args, plan, source, plan.atom_begin + item.x, item.y, ps, ws);
+                emit_pair(args, out_row + lane, source, plan.atom_begin + item.x, cand.shift,
+                          cand.vec);
+            }
+            __syncwarp();
+        } else {
+            if (lane == 0) {
+                args.counts[source] = count;
+                if (count > static_cast<uint32_t>(INT_MAX)) {
+                    atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
+                }
             }
         }
     }
 }
 
 int64_t blocks_for(int64_t items, int64_t per_block) { return (items + per_block - 1) / per_block; }
+
+// Grid for a grid-stride kernel: enough blocks to fill every SM at the
+// kernel's occupancy, never more than the work needs.
+template <typename Kernel>
+unsigned persistent_blocks(Kernel kernel, int threads, int64_t needed) {
+    int device = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
+    const int64_t full = static_cast<int64_t>(sms) * std::max(per_sm, 1);
+    return static_cast<unsigned>(std::max<int64_t>(1, std::min(needed, full)));
+}
 
 }  // namespace
 }  // namespace tnr
@@ -562,24 +880,42 @@ void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream) {
 }
 
 template <typename T>
+void launch_stencil_words(const SearchArgs<T>& args, unsigned long long* bin_words,
+                          cudaStream_t stream) {
+    if (args.n_bins == 0) return;
+    const unsigned blocks = persistent_blocks(stencil_words_kernel<T>, kBinThreads,
+                                              blocks_for(args.n_bins, kBinThreads / 32));
+    stencil_words_kernel<T><<<blocks, kBinThreads, 0, stream>>>(args, args.n_bins, bin_words);
+}
+
+template <typename T>
 void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stream) {
-    if (args.n_sources == 0) return;
-    const unsigned blocks = static_cast<unsigned>(blocks_for(args.n_sources, kSearchWarps));
+    if (args.n_sources == 0 || args.n_bins == 0) return;
+    const int64_t needed = blocks_for(args.n_bins, kSearchWarps);
     if (write) {
-        cell_search_kernel<T, true><<<blocks, kSearchThreads, 0, stream>>>(args);
+        cell_write_kernel<T><<<persistent_blocks(cell_write_kernel<T>, kSearchThreads, needed),
+                               kSearchThreads, 0, stream>>>(args);
+    } else if (args.half_list) {
+        cell_count_kernel<T, true><<<persistent_blocks(cell_count_kernel<T, true>, kSearchThreads,
+                                                       needed), kSearchThreads, 0, stream>>>(args);
     } else {
-        cell_search_kernel<T, false><<<blocks, kSearchThreads, 0, stream>>>(args);
+        cell_count_kernel<T, false><<<persistent_blocks(cell_count_kernel<T, false>, kSearchThreads,
+                                                        needed), kSearchThreads, 0, stream>>>(args);
     }
 }
 
 template <typename T>
 void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t stream) {
     if (args.n_brute_atoms == 0) return;
-    const unsigned blocks = static_cast<unsigned>(blocks_for(args.n_brute_atoms, kSearchWarps));
+    const int64_t needed = blocks_for(args.n_brute_atoms, kSearchWarps);
     if (write) {
-        brute_search_kernel<T, true><<<blocks, kSearchThreads, 0, stream>>>(args);
+        brute_search_kernel<T, true><<<persistent_blocks(brute_search_kernel<T, true>,
+                                                         kSearchThreads, needed),
+                                       kSearchThreads, 0, stream>>>(args);
     } else {
-        brute_search_kernel<T, false><<<blocks, kSearchThreads, 0, stream>>>(args);
+        brute_search_kernel<T, false><<<persistent_blocks(brute_search_kernel<T, false>,
+                                                          kSearchThreads, needed),
+                                        kSearchThreads, 0, stream>>>(args);
     }
 }
 
@@ -626,6 +962,8 @@ void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* works
     template void launch_prepare<T>(const PrepareArgs<T>&, cudaStream_t);                  \
     template void launch_bin<T>(const BinArgs<T>&, bool, cudaStream_t);                     \
     template void launch_cell_search<T>(const SearchArgs<T>&, bool, cudaStream_t);          \
+    template void launch_stencil_words<T>(const SearchArgs<T>&, unsigned long long*,      \
+                                          cudaStream_t);                                     \
     template void launch_brute_search<T>(const SearchArgs<T>&, bool, cudaStream_t);
 TNR_INSTANTIATE(float)
 TNR_INSTANTIATE(double)

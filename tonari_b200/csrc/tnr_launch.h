@@ -37,6 +37,8 @@ struct BinArgs {
     int32_t* self_slot;          // [N]             (scatter only)
     int32_t* source_list;        // [sources]       (scatter only)
     uint32_t* status;
+    const int4* image_shift;        // [images] (x, y, z, 0), x-major per structure
+    const void* image_translation;  // vec4_t<T> [images], shift . cell in T
 };
 
 template <typename T>
@@ -53,6 +55,13 @@ struct SearchArgs {
     const int32_t* self_slot;
     const int32_t* source_list;
     int64_t n_sources;
+    const int64_t* cell_bin_prefix;     // [n_cell + 1] first bin of each cell-list structure
+    const int32_t* cell_structs;        // [n_cell]
+    int32_t n_cell;
+    int64_t n_bins;
+    const unsigned long long* bin_word_start;  // [bins + 1] scan of per-bin mask words
+    uint32_t* mask_words;               // count pass ballots, read by the write pass
+    const int4* image_shift;            // [images]
     // brute mode
     const int64_t* brute_prefix;  // [n_brute + 1]
     const int32_t* brute_structs; // [n_brute]
@@ -78,6 +87,10 @@ void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream);
 
 template <typename T>
 void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream);
+
+template <typename T>
+void launch_stencil_words(const SearchArgs<T>& args, unsigned long long* bin_words,
+                          cudaStream_t stream);
 
 template <typename T>
 void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stream);

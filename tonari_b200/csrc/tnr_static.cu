@@ -172,12 +172,22 @@ void run_static(const tnr_request& request, cudaStream_t stream, int64_t capacit
         }
     }
     std::vector<Reduction<T>> reductions(static_cast<size_t>(batch), neutral<T>());
+    std::vector<int4> image_shift(static_cast<size_t>(std::max<int64_t>(geometry.image_begin[batch], 1)));
+    for (int64_t b = 0; b < batch; ++b) {
+        const int32_t* r = geometry.repeats.data() + 3 * b;
+        int64_t k = geometry.image_begin[b];
+        if (geometry.image_begin[b + 1] == k) continue;
+        for (int32_t x = -r[0]; x <= r[0]; ++x)
+            for (int32_t y = -r[1]; y <= r[1]; ++y)
+                for (int32_t z = -r[2]; z <= r[2]; ++z) image_shift[k++] = make_int4(x, y, z, 0);
+    }
 
     auto* d_prepare = carve.take<PrepareStructure<T>>(prepare.size());
     auto* d_plans = carve.take<StructurePlan<T>>(plans.size());
     auto* d_reductions = carve.take<Reduction<T>>(reductions.size());
     auto* d_brute_structs = carve.take<int32_t>(brute_structs.size());
     auto* d_brute_prefix = carve.take<int64_t>(brute_prefix.size());
+    auto* d_image_shift = carve.take<int4>(image_shift.size());
     auto* d_atom_struct = carve.take<int32_t>(n_atoms);
     auto* d_wraps = carve.take<int32_t>(3 * n_atoms);
     auto* d_wrapped = carve.take<V4>(n_atoms);
@@ -201,6 +211,8 @@ void run_static(const tnr_request& request, cudaStream_t stream, int64_t capacit
     }
     check(cudaMemcpy(d_brute_prefix, brute_prefix.data(), brute_prefix.size() * sizeof(int64_t),
                      cudaMemcpyHostToDevice), "upload");
+    check(cudaMemcpy(d_image_shift, image_shift.data(), image_shift.size() * sizeof(int4),
+                     cudaMemcpyHostToDevice), "upload");
     // Scratch keeps the previous call's bytes: clear what must start at zero.
     check(cudaMemsetAsync(d_status, 0, 4 * sizeof(uint32_t), stream), "clear status");
     check(cudaMemsetAsync(d_counts, 0, n_atoms * sizeof(uint32_t), stream), "clear counts");
@@ -218,6 +230,7 @@ void run_static(const tnr_request& request, cudaStream_t stream, int64_t capacit
     search.wrapped = d_wrapped;
     search.plans = d_plans;
     search.brute_prefix = d_brute_prefix;
+    search.image_shift = d_image_shift;
     search.brute_structs = d_brute_structs;
     search.n_brute = static_cast<int32_t>(brute_structs.size());
     search.n_brute_atoms = brute_prefix.back();
