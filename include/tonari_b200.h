@@ -84,6 +84,8 @@ typedef struct {
     int32_t algorithm;        /* tnr_algorithm */
     uint32_t quantities;      /* OR of tnr_quantity */
     int64_t index_offset;     /* added to every emitted atom index (shards) */
+    int32_t sorted;           /* bool: pairs ordered by source index; when false the
+                                 order is unspecified (cell order, faster writes) */
 } tnr_request;
 
 typedef struct {
@@ -99,8 +101,9 @@ typedef struct {
 /*
  * Replaces tonari csrc/torch/bindings_cuda.cpp:59 `neighbor_list`
  * (positions, batch_ptr, cell, pbc, cutoff, half_list, include_self,
- * algorithm, sorted).  Pairs are always emitted source-major (sorted by
- * source index), so the reference's `sorted` option is satisfied for free.
+ * algorithm, sorted).  With request->sorted the pairs of each source are
+ * contiguous and sources ascend; without it the order is unspecified, as in
+ * the reference, and pairs are written in cell order (faster).
  * Work is enqueued on `stream`; the call returns after the pair count is
  * known and the write pass has been enqueued (outputs are ready in stream
  * order).  On error `message` receives the reference's error text.

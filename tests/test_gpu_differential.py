@@ -154,7 +154,8 @@ def test_benchmark_configs_match_oracle(name):
                         sorted=w.options.get("sorted", False),
                         half_list=w.options.get("half_list", False))
     pairs, shifts = out[-2], out[-1]
-    assert_sorted_by_source(pairs)
+    if w.options.get("sorted", False):
+        assert_sorted_by_source(pairs)
     assert_same_pairs(pairs, shifts, *expected_pairs(w.positions, w.cell, w.pbc, w.cutoff,
                                                      w.batch_ptr,
                                                      half_list=w.options.get("half_list", False)))
@@ -184,3 +185,17 @@ def test_cfg4_reduced_cell_list_matches_oracle():
     assert_same_pairs(pairs, S, *expected_pairs(w.positions, w.cell, w.pbc, w.cutoff, w.batch_ptr))
     check_vectors(w.positions, w.cell, w.batch_ptr, pairs.cpu().numpy(), S.cpu().numpy(),
                   d.cpu().numpy(), D.cpu().numpy(), w.cutoff)
+
+
+@pytest.mark.parametrize("half_list", [False, True])
+def test_sorted_and_unsorted_orders_hold_the_same_pairs(half_list):
+    w = workloads.config4(n_atoms=30_000)
+    positions, cell, pbc, batch_ptr = w.torch_inputs("cuda")
+    unsorted = neighbor_list("PSdD", positions, cell, pbc, w.cutoff, batch_ptr,
+                             half_list=half_list)
+    ordered = neighbor_list("PSdD", positions, cell, pbc, w.cutoff, batch_ptr, sorted=True,
+                            half_list=half_list)
+    assert_sorted_by_source(ordered[0])
+    assert_same_pairs(unsorted[0], unsorted[1], ordered[0], ordered[1])
+    a = canonical(unsorted[0], unsorted[1])
+    assert len(a) > 0

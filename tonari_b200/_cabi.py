@@ -22,6 +22,7 @@ class Request(ctypes.Structure):
         ("cutoff", ctypes.c_double), ("half_list", ctypes.c_int32),
         ("include_self", ctypes.c_int32), ("algorithm", ctypes.c_int32),
         ("quantities", ctypes.c_uint32), ("index_offset", ctypes.c_int64),
+        ("sorted", ctypes.c_int32),
     ]
 
 

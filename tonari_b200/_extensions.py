@@ -10,7 +10,11 @@ from __future__ import annotations
 from functools import lru_cache
 from pathlib import Path
 
-_LIB = Path(__file__).resolve().parent / "_lib"
+import os
+
+# TONARI_B200_LIB_DIR points the loader at another build of the two libraries
+# (used to compare builds side by side); default: the in-tree _lib directory.
+_LIB = Path(os.environ.get("TONARI_B200_LIB_DIR", Path(__file__).resolve().parent / "_lib"))
 CORE_LIBRARY = _LIB / "libtonari_b200.so"
 TORCH_LIBRARY = _LIB / "libtonari_b200_torch.so"
 

@@ -592,7 +592,13 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     bin_args.status = d_status;
     bin_args.image_shift = reinterpret_cast<const int4*>(second_device + off_image_shift);
     bin_args.image_translation = second_device + off_image_translation;
+    int32_t* d_bin_struct = nullptr;
+    V4* d_ghost_orig = nullptr;
     if (n_cell_atoms > 0) {
+        d_bin_struct = workspace.get<int32_t>(total_bins);
+        launch_bin_struct<T>(reinterpret_cast<const int64_t*>(second_device + off_cell_bins),
+                             bin_args.cell_structs, bin_args.n_cell, d_bin_struct, stream);
+        check_launch("bin structure kernel");
         auto* d_bin_counts = workspace.get<unsigned long long>(total_bins);
         d_bin_start = workspace.get<unsigned long long>(total_bins + 1);
         auto* d_cursor = workspace.get<unsigned long long>(total_bins + 1);
@@ -613,6 +619,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         words_args.cell_structs = bin_args.cell_structs;
         words_args.n_cell = bin_args.n_cell;
         words_args.n_bins = total_bins;
+        words_args.bin_struct = d_bin_struct;
         auto* d_bin_words = workspace.get<unsigned long long>(total_bins);
         d_bin_word_start = workspace.get<unsigned long long>(total_bins + 1);
         launch_stencil_words(words_args, d_bin_words, stream);
@@ -637,11 +644,14 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                        "cell-list image copies exceed int32 indexing");
         d_ghost_pos = workspace.get<V4>(ghosts);
         d_ghost_meta = workspace.get<int4>(ghosts);
+        d_ghost_orig = workspace.get<V4>(ghosts);
         d_self_slot = workspace.get<int32_t>(n_atoms);
         d_source_list = workspace.get<int32_t>(n_cell_atoms);
         bin_args.bin_counts = d_cursor;
         bin_args.ghost_pos = d_ghost_pos;
         bin_args.ghost_meta = d_ghost_meta;
+        bin_args.ghost_orig = d_ghost_orig;
+        bin_args.positions = static_cast<const T*>(request.positions);
         bin_args.self_slot = d_self_slot;
         bin_args.source_list = d_source_list;
         launch_bin(bin_args, true, stream);
@@ -672,6 +682,9 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.cell_structs = reinterpret_cast<const int32_t*>(second_device + off_cell_structs);
     search.n_cell = static_cast<int32_t>(cell_structs.size());
     search.n_bins = total_bins;
+    search.bin_struct = d_bin_struct;
+    search.ghost_orig = d_ghost_orig;
+    search.source_order = request.sorted ? 0 : 1;
     search.brute_prefix = reinterpret_cast<const int64_t*>(second_device + off_brute_prefix);
     search.brute_structs = reinterpret_cast<const int32_t*>(second_device + off_brute_structs);
     search.n_brute = static_cast<int32_t>(brute_structs.size());

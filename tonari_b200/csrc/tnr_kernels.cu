@@ -276,6 +276,12 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
             record.z = g[2];
             record.w = index_to_lane(static_cast<int32_t>(atom), T(0));
             reinterpret_cast<V*>(args.ghost_pos)[slot] = record;
+            V original;
+            original.x = args.positions[3 * atom];
+            original.y = args.positions[3 * atom + 1];
+            original.z = args.positions[3 * atom + 2];
+            original.w = record.w;
+            reinterpret_cast<V*>(args.ghost_orig)[slot] = original;
             const int4 image = args.image_shift[plan.image_begin + k];
             args.ghost_meta[slot] = make_int4(image.x - wrap[0], image.y - wrap[1],
                                               image.z - wrap[2], static_cast<int32_t>(atom));
@@ -398,6 +404,24 @@ __device__ __forceinline__ int32_t load_stencil(const StructurePlan<T>& plan,
     return total;
 }
 
+// Position of the (n+1)-th set bit of w (0 <= n < popc(w)), by halving.
+__device__ __forceinline__ int32_t nth_set_bit(uint32_t w, int32_t n) {
+    int32_t position = 0;
+#pragma unroll
+    for (int width = 16; width > 0; width >>= 1) {
+        const uint32_t low = w & ((1u << width) - 1u);
+        const int32_t c = __popc(low);
+        if (n >= c) {
+            n -= c;
+            w >>= width;
+            position += width;
+        } else {
+            w = low;
+        }
+    }
+    return position;
+}
+
 // Slot of candidate index k (0 <= k < total): the last row whose prefix is
 // <= k, found in four fixed steps.
 __device__ __forceinline__ int32_t slot_of(const StencilRows& rows, int32_t k) {
@@ -442,8 +466,7 @@ __global__ void __launch_bounds__(kBinThreads) stencil_words_kernel(SearchArgs<T
             if (lane == 0) bin_words[bin] = 0;
             continue;
         }
-        const int32_t c = segment_of(args.cell_bin_prefix, args.n_cell, bin);
-        const StructurePlan<T>& plan = args.plans[args.cell_structs[c]];
+        const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
         int32_t bx, by, bz;
         bin_coordinates(plan, bin, bx, by, bz);
         const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz,
@@ -475,8 +498,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
         const uint32_t first_source = static_cast<uint32_t>(args.bin_start[bin] >> 32);
         const uint32_t n_sources = static_cast<uint32_t>(args.bin_start[bin + 1] >> 32) - first_source;
         if (n_sources == 0) continue;
-        const int32_t c = segment_of(args.cell_bin_prefix, args.n_cell, bin);
-        const StructurePlan<T>& plan = args.plans[args.cell_structs[c]];
+        const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
         int32_t bx, by, bz;
         bin_coordinates(plan, bin, bx, by, bz);
         StencilRows& rows = stencil[warp];
@@ -582,7 +604,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 count += __popc(bits);
             }
             if (active && my_group == 0) {
-                args.counts[source] = count;
+                args.counts[args.source_order ? static_cast<int64_t>(first_source + rank) : source] = count;
                 if (count > static_cast<uint32_t>(INT_MAX)) {
                     atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
                 }
@@ -591,109 +613,195 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
     }
 }
 
-// Write pass: replays the candidate walk, reading the count pass's ballots
-// instead of recomputing distances, and queues accepted slots in shared
-// memory; every 32 queued pairs are emitted by the whole warp at once
-// (record loads, exact displacement, 32 consecutive output rows).
+// Write pass.  The warp replays the count pass's ballots for the sources of
+// its bin (32 at a time; each lane first loads one source's data into shared
+// memory) and queues accepted (candidate, source) entries.  Every 32 entries
+// the whole warp emits 32 consecutive output rows: each lane loads its
+// candidate's records (the ghost's shift and the target's original position
+// are stored with the ghost, so no dependent gather follows), evaluates the
+// public displacement, and the 12-byte S / D rows are staged in shared memory
+// so that every global store instruction is a contiguous 128-byte run.
+// Unsorted calls write pairs in cell order, so one bin is one contiguous
+// output range and the queue streams across its sources; sorted calls write
+// each source's pairs at its own offset and flush at source boundaries.
 template <typename T>
-__device__ __forceinline__ void emit_queued(const SearchArgs<T>& args, const StructurePlan<T>& plan,
-                                            int32_t source, const long long (&ws)[3],
-                                            int32_t slot, int64_t row_out, bool active,
+struct WriteShared {
+    int32_t queue_k[64];
+    uint8_t queue_r[64];
+    vec4_t<T> source_pos[32];  // original source position, w = source index
+    int4 source_wrap[32];
+    int32_t stage_S[96];
+    T stage_D[96];
+};
+
+template <typename T>
+__device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const StructurePlan<T>& plan,
+                                            const StencilRows& rows, WriteShared<T>& sh,
+                                            int32_t n, int64_t out_row, int lane,
                                             bool need_shift, bool need_vector) {
-    if (!active) return;
-    const int4 meta = args.ghost_meta[slot];
-    const int32_t target = meta.w;
-    long long shift[3] = {0, 0, 0};
-    if (need_shift) {
-        shift[0] = meta.x + ws[0];
-        shift[1] = meta.y + ws[1];
-        shift[2] = meta.z + ws[2];
-    }
+    using V = vec4_t<T>;
+    __syncwarp();
+    int32_t shift[3] = {0, 0, 0};
     T vec[3] = {T(0), T(0), T(0)};
-    if (need_vector) exact_displacement(args.positions, source, target, shift, plan.cell, vec);
-    emit_pair(args, row_out, source, target, shift, vec);
+    int64_t source = 0, target = 0;
+    if (lane < n) {
+        const int32_t slot = sh.queue_k[lane];
+        const int r = sh.queue_r[lane];
+        const V ps = sh.source_pos[r];
+        source = lane_to_index(ps.w);
+        if (need_shift || need_vector) {
+            const int4 meta = args.ghost_meta[slot];
+            const int4 ws = sh.source_wrap[r];
+            target = meta.w;
+            // Cell-list shifts fit int32 by construction of the plan.
+            shift[0] = meta.x + ws.x;
+            shift[1] = meta.y + ws.y;
+            shift[2] = meta.z + ws.z;
+            if (need_vector) {
+                const V pt = reinterpret_cast<const V*>(args.ghost_orig)[slot];
+                const T s0 = static_cast<T>(shift[0]);
+                const T s1 = static_cast<T>(shift[1]);
+                const T s2 = static_cast<T>(shift[2]);
+                const T* cell = plan.cell;
+                vec[0] = add_rn(add_rn(add_rn(sub_rn(pt.x, ps.x), mul_rn(s0, cell[0])),
+                                       mul_rn(s1, cell[3])), mul_rn(s2, cell[6]));
+                vec[1] = add_rn(add_rn(add_rn(sub_rn(pt.y, ps.y), mul_rn(s0, cell[1])),
+                                       mul_rn(s1, cell[4])), mul_rn(s2, cell[7]));
+                vec[2] = add_rn(add_rn(add_rn(sub_rn(pt.z, ps.z), mul_rn(s0, cell[2])),
+                                       mul_rn(s1, cell[5])), mul_rn(s2, cell[8]));
+            }
+        } else {
+            target = lane_to_index(reinterpret_cast<const V*>(args.ghost_pos)[slot].w);
+        }
+        const int64_t o = out_row + lane;
+        const int64_t s = source + args.index_offset;
+        const int64_t t = target + args.index_offset;
+        if (args.out_i) args.out_i[o] = s;
+        if (args.out_j) args.out_j[o] = t;
+        if (args.out_P) reinterpret_cast<longlong2*>(args.out_P)[o] = make_longlong2(s, t);
+        if (args.out_d) args.out_d[o] = sqrt(exact_norm2(vec[0], vec[1], vec[2]));
+        if (args.out_S) {
+            sh.stage_S[3 * lane] = shift[0];
+            sh.stage_S[3 * lane + 1] = shift[1];
+            sh.stage_S[3 * lane + 2] = shift[2];
+        }
+        if (args.out_D) {
+            sh.stage_D[3 * lane] = vec[0];
+            sh.stage_D[3 * lane + 1] = vec[1];
+            sh.stage_D[3 * lane + 2] = vec[2];
+        }
+    }
+    __syncwarp();
+    const int32_t words = 3 * n;
+    if (args.out_S) {
+        int32_t* out = args.out_S + 3 * out_row;
+#pragma unroll
+        for (int m = 0; m < 3; ++m) {
+            const int32_t e = lane + 32 * m;
+            if (e < words) out[e] = sh.stage_S[e];
+        }
+    }
+    if (args.out_D) {
+        T* out = args.out_D + 3 * out_row;
+#pragma unroll
+        for (int m = 0; m < 3; ++m) {
+            const int32_t e = lane + 32 * m;
+            if (e < words) out[e] = sh.stage_D[e];
+        }
+    }
+    __syncwarp();
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T> args) {
+    using V = vec4_t<T>;
     __shared__ StencilRows stencil[kSearchWarps];
-    __shared__ int32_t queue[kSearchWarps][64];
+    __shared__ WriteShared<T> shared[kSearchWarps];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const bool need_vector = args.out_d != nullptr || args.out_D != nullptr;
+    const bool need_shift = args.out_S != nullptr;
+    const bool by_atom = args.source_order == 0;
+    WriteShared<T>& sh = shared[warp];
     const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
     for (int64_t bin = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
          bin < args.n_bins; bin += stride) {
         const uint32_t first_source = static_cast<uint32_t>(args.bin_start[bin] >> 32);
-        const uint32_t last_source = static_cast<uint32_t>(args.bin_start[bin + 1] >> 32);
-        if (first_source == last_source) continue;
-        const int32_t c = segment_of(args.cell_bin_prefix, args.n_cell, bin);
-        const StructurePlan<T>& plan = args.plans[args.cell_structs[c]];
+        const uint32_t n_bin_sources =
+            static_cast<uint32_t>(args.bin_start[bin + 1] >> 32) - first_source;
+        if (n_bin_sources == 0) continue;
+        const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
         int32_t bx, by, bz;
         bin_coordinates(plan, bin, bx, by, bz);
         StencilRows& rows = stencil[warp];
         const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz, &rows, lane);
         const int32_t words = (total + 31) >> 5;
-        const unsigned long long word_base = args.bin_word_start[bin];
-        const bool need_vector = args.out_d != nullptr || args.out_D != nullptr;
-        const bool need_shift = need_vector || args.out_S != nullptr;
-        const unsigned below = (1u << lane) - 1u;
-        int32_t* q = queue[warp];
+        const uint32_t* bin_mask = args.mask_words + args.bin_word_start[bin];
+        int64_t out_row = by_atom ? 0 : args.pair_start[first_source];
 
-        const uint32_t n_bin_sources = last_source - first_source;
         for (uint32_t base = 0; base < n_bin_sources; base += 32) {
-            // One lane per source fetches that source's data; the warp then
-            // serves the sources one after another from registers.
             const uint32_t mine = base + lane;
-            int32_t my_source = 0, my_count = 0;
             int64_t my_start = 0;
-            int32_t my_wrap[3] = {0, 0, 0};
+            __syncwarp();
             if (mine < n_bin_sources) {
-                my_source = args.source_list[first_source + mine];
-                my_count = static_cast<int32_t>(args.counts[my_source]);
-                my_start = args.pair_start[my_source];
-                my_wrap[0] = args.wraps[3 * my_source];
-                my_wrap[1] = args.wraps[3 * my_source + 1];
-                my_wrap[2] = args.wraps[3 * my_source + 2];
+                const int32_t source = args.source_list[first_source + mine];
+                if (by_atom) my_start = args.pair_start[source];
+                V ps;
+                ps.x = args.positions[3 * source];
+                ps.y = args.positions[3 * source + 1];
+                ps.z = args.positions[3 * source + 2];
+                ps.w = index_to_lane(source, T(0));
+                sh.source_pos[lane] = ps;
+                sh.source_wrap[lane] = make_int4(args.wraps[3 * source], args.wraps[3 * source + 1],
+                                                 args.wraps[3 * source + 2], 0);
             }
-            const uint32_t batch = min(32u, n_bin_sources - base);
-            for (uint32_t b = 0; b < batch; ++b) {
-                if (__shfl_sync(kFullMask, my_count, b) == 0) continue;
-                const int32_t source = __shfl_sync(kFullMask, my_source, b);
-                int64_t out_row = __shfl_sync(kFullMask, my_start, b);
-                const long long ws[3] = {__shfl_sync(kFullMask, my_wrap[0], b),
-                                         __shfl_sync(kFullMask, my_wrap[1], b),
-                                         __shfl_sync(kFullMask, my_wrap[2], b)};
-                const uint32_t* mask = args.mask_words + word_base + base + b;
-                int32_t queued = 0;
-                for (int32_t chunk = 0; chunk < words; chunk += 32) {
-                    const uint32_t my_word =
-                        chunk + lane < words
-                            ? mask[static_cast<int64_t>(chunk + lane) * n_bin_sources] : 0u;
-                    const int32_t span = min(32, words - chunk);
-                    for (int32_t j = 0; j < span; ++j) {
-                        const uint32_t word = __shfl_sync(kFullMask, my_word, j);
-                        if (word != 0u) {
-                            if ((word >> lane) & 1u) {
-                                q[queued + __popc(word & below)] = 32 * (chunk + j) + lane;
-                            }
-                            queued += __popc(word);
-                            if (queued >= 32) {
-                                __syncwarp();
-                                emit_queued(args, plan, source, ws, slot_of(rows, q[lane]),
-                                            out_row + lane, true, need_shift, need_vector);
-                                __syncwarp();
-                                if (lane < queued - 32) q[lane] = q[32 + lane];
-                                __syncwarp();
-                                queued -= 32;
-                                out_row += 32;
-                            }
-                        }
+            __syncwarp();
+            const int32_t group = static_cast<int32_t>(min(32u, n_bin_sources - base));
+            // Items are (source, word) pairs.  Unsorted: all items of the
+            // group form one flat sequence and their pairs are consecutive
+            // rows.  Sorted: one source at a time, rows from its own start.
+            const int32_t passes = by_atom ? group : 1;
+            const int32_t n_items = by_atom ? words : group * words;
+            for (int32_t pass = 0; pass < passes; ++pass) {
+                if (by_atom) out_row = __shfl_sync(kFullMask, my_start, pass);
+                for (int32_t item0 = 0; item0 < n_items; item0 += 32) {
+                    const int32_t item = item0 + lane;
+                    int32_t r = pass, w = item;
+                    if (!by_atom) {
+                        r = item / words;
+                        w = item - r * words;
                     }
+                    const uint32_t word = item < n_items
+                        ? bin_mask[static_cast<int64_t>(w) * n_bin_sources + base + r] : 0u;
+                    const int32_t count = __popc(word);
+                    const int32_t inclusive = warp_inclusive_sum(count);
+                    const int32_t exclusive = inclusive - count;
+                    const int32_t produced = __shfl_sync(kFullMask, inclusive, 31);
+                    for (int32_t i = 0; i < produced; i += 32) {
+                        const int32_t g = i + lane;
+                        // Lane holding the item of pair g: the last lane
+                        // whose exclusive offset is <= g.
+                        int32_t at = 0;
+#pragma unroll
+                        for (int step = 16; step > 0; step >>= 1) {
+                            const int32_t probe = __shfl_sync(kFullMask, exclusive, at + step);
+                            if (probe <= g) at += step;
+                        }
+                        const uint32_t item_word = __shfl_sync(kFullMask, word, at);
+                        const int32_t item_start = __shfl_sync(kFullMask, exclusive, at);
+                        const int32_t item_r = __shfl_sync(kFullMask, r, at);
+                        const int32_t item_w = __shfl_sync(kFullMask, w, at);
+                        const int32_t n = min(32, produced - i);
+                        if (g < produced) {
+                            const int32_t bit = nth_set_bit(item_word, g - item_start);
+                            sh.queue_k[lane] = slot_of(rows, 32 * item_w + bit);
+                            sh.queue_r[lane] = static_cast<uint8_t>(item_r);
+                        }
+                        flush_queue(args, plan, rows, sh, n, out_row + i, lane, need_shift,
+                                    need_vector);
+                    }
+                    out_row += produced;
                 }
-                __syncwarp();
-                emit_queued(args, plan, source, ws, lane < queued ? slot_of(rows, q[lane]) : 0,
-                            out_row + lane, lane < queued, need_shift, need_vector);
-                __syncwarp();
             }
         }
     }
@@ -755,8 +863,9 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
         const int32_t c = segment_of(args.brute_prefix, args.n_brute, work);
         const StructurePlan<T>& plan = args.plans[args.brute_structs[c]];
         const int64_t source = plan.atom_begin + (work - args.brute_prefix[c]);
-        if constexpr (Write) {
-            if (args.counts[source] == 0) continue;
+        const int64_t order = args.source_order ? args.n_sources + work : source;
+            if constexpr (Write) {
+                if (args.counts[order] == 0) continue;
         }
         const T ps[3] = {args.positions[3 * source], args.positions[3 * source + 1],
                          args.positions[3 * source + 2]};
@@ -771,7 +880,7 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
         uint32_t count = 0;
         int64_t out_row = 0;
         int32_t queued = 0;
-        if constexpr (Write) out_row = args.pair_start[source];
+        if constexpr (Write) out_row = args.pair_start[order];
         // Warp-uniform trip count: ceil(n * images / 32) iterations.
         const int64_t trips = (static_cast<int64_t>(n) * images + 31) / 32;
         for (int64_t trip = 0; trip < trips; ++trip) {
@@ -830,13 +939,25 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
             __syncwarp();
         } else {
             if (lane == 0) {
-                args.counts[source] = count;
+                args.counts[order] = count;
                 if (count > static_cast<uint32_t>(INT_MAX)) {
                     atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
                 }
             }
         }
     }
+}
+
+// One block per cell-list structure writes that structure's index into its
+// bins' slots of bin_struct.
+__global__ void bin_struct_kernel(const int64_t* __restrict__ cell_bin_prefix,
+                                  const int32_t* __restrict__ cell_structs,
+                                  int32_t* __restrict__ bin_struct) {
+    const int32_t c = blockIdx.x;
+    const int64_t begin = cell_bin_prefix[c];
+    const int64_t end = cell_bin_prefix[c + 1];
+    const int32_t value = cell_structs[c];
+    for (int64_t bin = begin + threadIdx.x; bin < end; bin += blockDim.x) bin_struct[bin] = value;
 }
 
 int64_t blocks_for(int64_t items, int64_t per_block) { return (items + per_block - 1) / per_block; }
@@ -877,6 +998,14 @@ void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream) {
     } else {
         bin_kernel<T, false><<<blocks, kBinThreads, 0, stream>>>(args);
     }
+}
+
+template <typename T>
+void launch_bin_struct(const int64_t* cell_bin_prefix, const int32_t* cell_structs,
+                       int32_t n_cell, int32_t* bin_struct, cudaStream_t stream) {
+    if (n_cell == 0) return;
+    bin_struct_kernel<<<static_cast<unsigned>(n_cell), 256, 0, stream>>>(cell_bin_prefix,
+                                                                        cell_structs, bin_struct);
 }
 
 template <typename T>
@@ -961,6 +1090,8 @@ void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* works
 #define TNR_INSTANTIATE(T)                                                                 \
     template void launch_prepare<T>(const PrepareArgs<T>&, cudaStream_t);                  \
     template void launch_bin<T>(const BinArgs<T>&, bool, cudaStream_t);                     \
+    template void launch_bin_struct<T>(const int64_t*, const int32_t*, int32_t, int32_t*,    \
+                                       cudaStream_t);                                        \
     template void launch_cell_search<T>(const SearchArgs<T>&, bool, cudaStream_t);          \
     template void launch_stencil_words<T>(const SearchArgs<T>&, unsigned long long*,      \
                                           cudaStream_t);                                     \

@@ -34,6 +34,8 @@ struct BinArgs {
     unsigned long long* bin_counts;  // histogram target / scatter cursors
     void* ghost_pos;             // vec4_t<T> [G]   (scatter only)
     int4* ghost_meta;            // [G]             (scatter only)
+    void* ghost_orig;            // vec4_t<T> [G]   (scatter only)
+    const T* positions;
     int32_t* self_slot;          // [N]             (scatter only)
     int32_t* source_list;        // [sources]       (scatter only)
     uint32_t* status;
@@ -55,6 +57,9 @@ struct SearchArgs {
     const int32_t* self_slot;
     const int32_t* source_list;
     int64_t n_sources;
+    const int32_t* bin_struct;          // [bins] structure of each bin
+    const void* ghost_orig;             // vec4_t<T> [G] original target position, target
+    int32_t source_order;               // 0: outputs by atom index; 1: cell order
     const int64_t* cell_bin_prefix;     // [n_cell + 1] first bin of each cell-list structure
     const int32_t* cell_structs;        // [n_cell]
     int32_t n_cell;
@@ -87,6 +92,11 @@ void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream);
 
 template <typename T>
 void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream);
+
+// Writes the structure index of every cell-list bin.
+template <typename T>
+void launch_bin_struct(const int64_t* cell_bin_prefix, const int32_t* cell_structs,
+                       int32_t n_cell, int32_t* bin_struct, cudaStream_t stream);
 
 template <typename T>
 void launch_stencil_words(const SearchArgs<T>& args, unsigned long long* bin_words,

@@ -86,7 +86,6 @@ std::vector<at::Tensor> neighbor_list_cuda(const at::Tensor& positions, const at
                                            double cutoff, bool half_list, bool include_self,
                                            std::string algorithm, bool sorted,
                                            std::string quantities, int64_t index_offset) {
-    (void)sorted;  // output is always source-major
     TORCH_CHECK(positions.is_cuda(), "positions must be a CUDA tensor");
     TORCH_CHECK(batch_ptr.is_cuda() && cell.is_cuda() && pbc.is_cuda(),
                 "all inputs must be CUDA tensors");
@@ -128,6 +127,7 @@ std::vector<at::Tensor> neighbor_list_cuda(const at::Tensor& positions, const at
     request.algorithm = parse_algorithm(algorithm);
     request.quantities = parse_quantities(quantities);
     request.index_offset = index_offset;
+    request.sorted = sorted;
 
     TorchAllocator context{positions.device(), {}};
     tnr_allocator allocator{&context, torch_allocate, torch_release};
