@@ -5,8 +5,10 @@
 
 Workload (default cfg5, tonari_b200/workloads.py): 8192 triclinic structures,
 50-5000 atoms, mixed pbc, float32, cutoff 5, half list, 'PS'.  Scaling is
-weak: rank r processes its own seeded cfg5 batch (seed 5 + r), with no
-collective on the data path; value = pairs of all ranks / max-over-ranks time.
+weak: with N ranks the global batch is N seeded cfg5 batches, split into N
+contiguous shards balanced by estimated pair count (tonari_b200.sharding);
+no collective on the data path; value = pairs of all ranks / max-over-ranks
+time.
 
 A step is one neighbor_list call over the whole batch.
 * value: inputs already in HBM, device time per step from CUDA events on the
@@ -63,11 +65,26 @@ def peak_hbm():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def make_workload(name: str, rank: int):
-    from tonari_b200 import workloads
+SEEDS = {"cfg1": 0, "cfg2": 2, "cfg3": 3, "cfg4": 4, "cfg5": 5}
 
-    seeds = {"cfg1": 0, "cfg2": 2, "cfg3": 3, "cfg4": 4, "cfg5": 5}
-    return workloads.CONFIGS[name](seed=seeds[name] + rank)
+
+def make_workload(name: str, rank: int, world: int = 1):
+    """The rank's share of the job.  N=1: the configuration itself.  N>1
+    (weak scaling): the global batch is N seeded copies of the configuration
+    (seeds s, s+1, ...), split into N contiguous shards balanced by estimated
+    pair count (tonari_b200.sharding); a single structure is never split."""
+    from tonari_b200 import sharding, workloads
+
+    if world == 1:
+        return workloads.CONFIGS[name](seed=SEEDS[name])
+    parts = [workloads.CONFIGS[name](seed=SEEDS[name] + k) for k in range(world)]
+    whole = workloads.concatenate(parts, f"{name}x{world}")
+    weights = sharding.estimate_pairs(whole.batch_ptr, whole.cell, whole.pbc, whole.cutoff,
+                                      half_list=whole.options.get("half_list", False))
+    shard = sharding.partition(whole.batch_ptr, weights, world)[rank]
+    part = whole.shard(shard.structure_begin, shard.structure_end)
+    part.name = f"{name}x{world}[rank {rank}]"
+    return part
 
 
 def call_kwargs(w):
@@ -135,8 +152,8 @@ def core_library():
 
 
 def phase_times(lib):
-    buffer = (ctypes.c_float * 5)()
-    lib.tnr_last_phase_times(buffer, 5)
+    buffer = (ctypes.c_float * 6)()
+    lib.tnr_last_phase_times(buffer, 6)
     return list(buffer)
 
 
@@ -167,7 +184,7 @@ def measure_device(w, steps, warmup, device):
             end.record(stream)
             end.synchronize()
             step_ms.append(start.elapsed_time(end))
-            write_ms.append(phase_times(lib)[4])
+            write_ms.append(phase_times(lib)[5])
             launches.append(int(lib.tnr_last_launch_count()))
             n_pairs = int(out[0].shape[0])
             del out
@@ -302,7 +319,7 @@ def main():
 
     load_torch_cuda()
 
-    w = make_workload(args.workload, rank)
+    w = make_workload(args.workload, rank, world)
 
     def barrier():
         if world > 1:
@@ -349,7 +366,8 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32" if w.positions.dtype == np.float32 else "f64", "data": "synthetic",
-        "config": {"workload": w.name, "structures_per_gpu": w.n_structures,
+        "config": {"workload": args.workload if world == 1 else f"{args.workload} x{world}",
+                   "structures_per_gpu": w.n_structures,
                    "atoms_per_gpu": w.n_atoms, "cutoff": w.cutoff, "quantities": w.quantities,
                    **call_kwargs(w), "pairs_per_step": int(pairs_all),
                    "l2": "flushed between steps (256 MiB write)",

@@ -140,8 +140,10 @@ const char* tnr_version(void);
 int64_t tnr_last_launch_count(void);
 
 /* Per-phase device times (ms) of the last call on this host thread when the
- * environment variable TONARI_B200_PHASE_TIMERS=1 is set, else zeros.
- * Order: prepare, bin, count, scan, write. Returns the number written. */
+ * environment variable TONARI_B200_PHASE_TIMERS=1 is set, else zeros, from
+ * CUDA events on the call's stream.  Order: prepare, bin, count kernels,
+ * count scan, pair-total readback + output allocation, write kernels.
+ * Returns the number written (at most 6). */
 int tnr_last_phase_times(float* times_ms, int capacity);
 
 #ifdef __cplusplus

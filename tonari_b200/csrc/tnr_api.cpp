@@ -35,8 +35,17 @@ namespace tnr {
 namespace {
 
 // Auto rule: a structure whose per-source candidate count (atoms x images)
-// is at most this takes the brute-force kernel.
-constexpr int64_t kBruteCandidatesPerSource = 2048;
+// is at most this takes the brute-force kernel; TONARI_B200_BRUTE_CANDIDATES
+// overrides it (a tuning knob; results do not depend on it).
+constexpr int64_t kBruteCandidatesPerSource = 256;
+
+int64_t brute_candidates_per_source() {
+    static const int64_t value = [] {
+        const char* text = std::getenv("TONARI_B200_BRUTE_CANDIDATES");
+        return text ? std::max<int64_t>(0, std::atoll(text)) : kBruteCandidatesPerSource;
+    }();
+    return value;
+}
 // The reference's bin-layout safety limits (tonari csrc/core/neighbors_cpu.cpp:23-24).
 constexpr int64_t kMaximumDenseBins = int64_t{1} << 26;
 constexpr int64_t kMaximumBinsPerImage = 64;
@@ -45,7 +54,7 @@ constexpr int64_t kMaximumTotalBins = int64_t{1} << 28;
 constexpr int kRoundoffFactor = 64;
 
 thread_local int64_t g_launches = 0;
-thread_local float g_phase_ms[5] = {0, 0, 0, 0, 0};
+thread_local float g_phase_ms[6] = {0, 0, 0, 0, 0, 0};
 
 struct CudaError : std::runtime_error {
     using std::runtime_error::runtime_error;
@@ -157,34 +166,39 @@ private:
 
 thread_local Pinned g_pinned;
 
-// Packs several host arrays into one pinned block and one device block, then
-// uploads them with a single copy.
+// Packs several host arrays into a caller-provided pinned region (256-byte
+// aligned offsets) and uploads them with a single copy.
 class Upload {
 public:
+    explicit Upload(char* pinned, size_t capacity) : pinned_(pinned), capacity_(capacity) {}
     template <typename U>
     size_t add(const U* data, size_t count) {
-        const size_t offset = (bytes_.size() + 255) / 256 * 256;
-        bytes_.resize(offset + std::max<size_t>(count * sizeof(U), 1));
-        if (count) std::memcpy(bytes_.data() + offset, data, count * sizeof(U));
+        const size_t offset = (size_ + 255) / 256 * 256;
+        const size_t bytes = count * sizeof(U);
+        if (offset + std::max<size_t>(bytes, 1) > capacity_) {
+            throw std::runtime_error("internal error: upload staging overflow");
+        }
+        if (bytes) std::memcpy(pinned_ + offset, data, bytes);
+        size_ = offset + std::max<size_t>(bytes, 1);
         return offset;
     }
-    char* commit(Workspace& workspace, cudaStream_t stream, char* pinned_region) {
-        char* device = static_cast<char*>(workspace.raw(std::max<size_t>(bytes_.size(), 16)));
-        std::memcpy(pinned_region, bytes_.data(), bytes_.size());
-        check_cuda(cudaMemcpyAsync(device, pinned_region, bytes_.size(), cudaMemcpyHostToDevice,
-                                   stream), "upload");
+    char* commit(Workspace& workspace, cudaStream_t stream) {
+        char* device = static_cast<char*>(workspace.raw(std::max<size_t>(size_, 16)));
+        check_cuda(cudaMemcpyAsync(device, pinned_, size_, cudaMemcpyHostToDevice, stream),
+                   "upload");
         return device;
     }
-    size_t size() const { return bytes_.size(); }
 
 private:
-    std::vector<char> bytes_;
+    char* pinned_;
+    size_t capacity_;
+    size_t size_ = 0;
 };
 
 struct PhaseTimer {
     bool enabled = false;
     cudaStream_t stream = nullptr;
-    cudaEvent_t events[6] = {};
+    cudaEvent_t events[7] = {};
     int recorded = 0;
     explicit PhaseTimer(cudaStream_t s) : stream(s) {
         const char* flag = std::getenv("TONARI_B200_PHASE_TIMERS");
@@ -200,7 +214,7 @@ struct PhaseTimer {
         }
     }
     void mark(int index) {
-        if (enabled && index < 6) {
+        if (enabled && index < 7) {
             cudaEventRecord(events[index], stream);
             recorded = std::max(recorded, index + 1);
         }
@@ -208,7 +222,7 @@ struct PhaseTimer {
     void finish() {
         if (!enabled || recorded < 2) return;
         cudaEventSynchronize(events[recorded - 1]);
-        for (int k = 0; k + 1 < recorded && k < 5; ++k) {
+        for (int k = 0; k + 1 < recorded && k < 6; ++k) {
             cudaEventElapsedTime(&g_phase_ms[k], events[k], events[k + 1]);
         }
     }
@@ -393,7 +407,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         (sizeof(PrepareStructure<T>) + sizeof(Reduction<T>)) + 1024;
     const size_t plan_bytes = static_cast<size_t>(batch) *
         (sizeof(StructurePlan<T>) + 3 * sizeof(int64_t) + 2 * sizeof(int32_t)) +
-        static_cast<size_t>(geometry.image_begin[batch] + 1) * (sizeof(int4) + sizeof(V4)) +
         8192;
     const size_t read_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>) + 1024;
     char* pinned = g_pinned.reserve(prepare_bytes + plan_bytes + read_bytes);
@@ -413,10 +426,10 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         }
     }
     std::vector<Reduction<T>> reductions(static_cast<size_t>(batch), neutral_reduction<T>());
-    Upload first;
+    Upload first(pinned_prepare, prepare_bytes);
     const size_t off_prepare = first.add(prepare.data(), prepare.size());
     const size_t off_reduction = first.add(reductions.data(), reductions.size());
-    char* first_device = first.commit(workspace, stream, pinned_prepare);
+    char* first_device = first.commit(workspace, stream);
     auto* d_prepare = reinterpret_cast<PrepareStructure<T>*>(first_device + off_prepare);
     auto* d_reductions = reinterpret_cast<Reduction<T>*>(first_device + off_reduction);
 
@@ -447,7 +460,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         if (request.algorithm == TNR_CELL_LIST) {
             cell = true;
         } else if (request.algorithm == TNR_AUTO) {
-            cell = counts[b] > kBruteCandidatesPerSource / std::max<int64_t>(images, 1);
+            cell = counts[b] > brute_candidates_per_source() / std::max<int64_t>(images, 1);
         }
         mode[b] = cell ? kModeCell : kModeBrute;
         any_cell = any_cell || cell;
@@ -528,47 +541,14 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     std::vector<int64_t> cell_bin_prefix;
     for (int32_t b : cell_structs) cell_bin_prefix.push_back(plans[b].bin_begin);
     cell_bin_prefix.push_back(total_bins);
-    // Image tables: integer shifts enumerated x-major, then y, then z (the
-    // reference's order, tonari csrc/core/geometry.cpp:229-237), and their
-    // Cartesian translations evaluated once in T.
-    const int64_t total_images = geometry.image_begin[batch];
-    std::vector<int4> image_shift(static_cast<size_t>(std::max<int64_t>(total_images, 1)));
-    std::vector<V4> image_translation(image_shift.size());
-    for (int64_t b = 0; b < batch; ++b) {
-        const int32_t* r = geometry.repeats.data() + 3 * b;
-        const T* cell = cell_t.data() + 9 * b;
-        int64_t k = geometry.image_begin[b];
-        if (geometry.image_begin[b + 1] == k) continue;
-        for (int32_t x = -r[0]; x <= r[0]; ++x) {
-            for (int32_t y = -r[1]; y <= r[1]; ++y) {
-                for (int32_t z = -r[2]; z <= r[2]; ++z, ++k) {
-                    image_shift[k] = make_int4(x, y, z, 0);
-                    T t[3];
-                    for (int c = 0; c < 3; ++c) {
-                        volatile T value = T(0);  // evaluated in T, one rounding per operation
-                        value = value + static_cast<T>(x) * cell[c];
-                        value = value + static_cast<T>(y) * cell[3 + c];
-                        value = value + static_cast<T>(z) * cell[6 + c];
-                        t[c] = value;
-                    }
-                    image_translation[k].x = t[0];
-                    image_translation[k].y = t[1];
-                    image_translation[k].z = t[2];
-                    image_translation[k].w = T(0);
-                }
-            }
-        }
-    }
-    Upload second;
+    Upload second(pinned_plan, plan_bytes);
     const size_t off_plans = second.add(plans.data(), plans.size());
-    const size_t off_image_shift = second.add(image_shift.data(), image_shift.size());
-    const size_t off_image_translation = second.add(image_translation.data(), image_translation.size());
     const size_t off_cell_prefix = second.add(cell_prefix.data(), cell_prefix.size());
     const size_t off_cell_structs = second.add(cell_structs.data(), cell_structs.size());
     const size_t off_brute_prefix = second.add(brute_prefix.data(), brute_prefix.size());
     const size_t off_brute_structs = second.add(brute_structs.data(), brute_structs.size());
     const size_t off_cell_bins = second.add(cell_bin_prefix.data(), cell_bin_prefix.size());
-    char* second_device = second.commit(workspace, stream, pinned_plan);
+    char* second_device = second.commit(workspace, stream);
     auto* d_plans = reinterpret_cast<StructurePlan<T>*>(second_device + off_plans);
 
     // ---- cell list binning: histogram -> scan -> scatter ------------------
@@ -590,8 +570,13 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     bin_args.wraps = d_wraps;
     bin_args.wrapped = d_wrapped;
     bin_args.status = d_status;
-    bin_args.image_shift = reinterpret_cast<const int4*>(second_device + off_image_shift);
-    bin_args.image_translation = second_device + off_image_translation;
+    const int64_t total_images = geometry.image_begin[batch];
+    auto* d_image_shift = workspace.get<int4>(std::max<int64_t>(total_images, 1));
+    auto* d_image_translation = workspace.get<V4>(std::max<int64_t>(total_images, 1));
+    launch_image_table<T>(d_plans, batch, d_image_shift, d_image_translation, stream);
+    check_launch("image table kernel");
+    bin_args.image_shift = d_image_shift;
+    bin_args.image_translation = d_image_translation;
     int32_t* d_bin_struct = nullptr;
     V4* d_ghost_orig = nullptr;
     if (n_cell_atoms > 0) {
@@ -736,6 +721,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.out_S = result.S;
     search.out_d = static_cast<T*>(result.d);
     search.out_D = static_cast<T*>(result.D);
+    timer.mark(5);
     if (q != 0) {
         if (n_cell_atoms) {
             launch_cell_search(search, true, stream);
@@ -746,7 +732,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
             check_launch("brute write kernel");
         }
     }
-    timer.mark(5);
+    timer.mark(6);
     timer.finish();
 }
 
@@ -819,7 +805,7 @@ const char* tnr_version(void) { return "0.1.0"; }
 int64_t tnr_last_launch_count(void) { return tnr::g_launches; }
 
 int tnr_last_phase_times(float* times_ms, int capacity) {
-    const int count = std::min(capacity, 5);
+    const int count = std::min(capacity, 6);
     for (int k = 0; k < count; ++k) times_ms[k] = tnr::g_phase_ms[k];
     return count;
 }

@@ -948,6 +948,39 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
     }
 }
 
+// Image tables of one structure per block: integer shifts enumerated x-major,
+// then y, then z (tonari csrc/core/geometry.cpp:229-237), and their Cartesian
+// translations in T.  Only the binning passes read the translations, both
+// from this table, so they agree bit for bit.
+template <typename T>
+__global__ void image_table_kernel(const StructurePlan<T>* __restrict__ plans,
+                                   int4* __restrict__ shifts, void* translations_out) {
+    using V = vec4_t<T>;
+    const StructurePlan<T>& plan = plans[blockIdx.x];
+    V* translations = reinterpret_cast<V*>(translations_out);
+    for (int32_t k = threadIdx.x; k < plan.n_images; k += blockDim.x) {
+        int32_t image[3];
+        decode_image(k, plan.repeats, image);
+        shifts[plan.image_begin + k] = make_int4(image[0], image[1], image[2], 0);
+        V t;
+        T c[3];
+#pragma unroll
+        for (int axis = 0; axis < 3; ++axis) {
+            T value = T(0);
+#pragma unroll
+            for (int a = 0; a < 3; ++a) {
+                value = add_rn(value, mul_rn(static_cast<T>(image[a]), plan.cell[3 * a + axis]));
+            }
+            c[axis] = value;
+        }
+        t.x = c[0];
+        t.y = c[1];
+        t.z = c[2];
+        t.w = T(0);
+        translations[plan.image_begin + k] = t;
+    }
+}
+
 // One block per cell-list structure writes that structure's index into its
 // bins' slots of bin_struct.
 __global__ void bin_struct_kernel(const int64_t* __restrict__ cell_bin_prefix,
@@ -998,6 +1031,14 @@ void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream) {
     } else {
         bin_kernel<T, false><<<blocks, kBinThreads, 0, stream>>>(args);
     }
+}
+
+template <typename T>
+void launch_image_table(const StructurePlan<T>* plans, int64_t batch, int4* shifts,
+                        void* translations, cudaStream_t stream) {
+    if (batch == 0) return;
+    image_table_kernel<T><<<static_cast<unsigned>(batch), 128, 0, stream>>>(plans, shifts,
+                                                                          translations);
 }
 
 template <typename T>
@@ -1090,6 +1131,8 @@ void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* works
 #define TNR_INSTANTIATE(T)                                                                 \
     template void launch_prepare<T>(const PrepareArgs<T>&, cudaStream_t);                  \
     template void launch_bin<T>(const BinArgs<T>&, bool, cudaStream_t);                     \
+    template void launch_image_table<T>(const StructurePlan<T>*, int64_t, int4*, void*,    \
+                                        cudaStream_t);                                       \
     template void launch_bin_struct<T>(const int64_t*, const int32_t*, int32_t, int32_t*,    \
                                        cudaStream_t);                                        \
     template void launch_cell_search<T>(const SearchArgs<T>&, bool, cudaStream_t);          \

@@ -93,6 +93,11 @@ void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream);
 template <typename T>
 void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream);
 
+// Fills the per-structure image tables (shift, translation) on the device.
+template <typename T>
+void launch_image_table(const StructurePlan<T>* plans, int64_t batch, int4* shifts,
+                        void* translations, cudaStream_t stream);
+
 // Writes the structure index of every cell-list bin.
 template <typename T>
 void launch_bin_struct(const int64_t* cell_bin_prefix, const int32_t* cell_structs,

@@ -179,3 +179,14 @@ def algorithmic_bytes(workload: Workload, n_pairs: int) -> int:
     read = (workload.n_atoms * 3 * s + workload.n_structures * 9 * s
             + workload.n_structures * 3 + (workload.n_structures + 1) * 8)
     return int(read + n_pairs * sum(per_pair[q] for q in set(workload.quantities)))
+
+
+def concatenate(parts: list[Workload], name: str) -> Workload:
+    """One batch made of several workloads' structures, in order."""
+    offsets = np.cumsum([0] + [p.n_atoms for p in parts])
+    batch_ptr = np.concatenate([parts[0].batch_ptr[:1]] +
+                               [p.batch_ptr[1:] + o for p, o in zip(parts, offsets)])
+    return Workload(name, np.concatenate([p.positions for p in parts]),
+                    np.concatenate([p.cell for p in parts]), np.concatenate([p.pbc for p in parts]),
+                    batch_ptr.astype(np.int64), parts[0].cutoff, parts[0].quantities,
+                    dict(parts[0].options))
