@@ -433,23 +433,6 @@ __device__ __forceinline__ int32_t slot_of(const StencilRows& rows, int32_t k) {
     return k + rows.delta[r];
 }
 
-// Exact decision for the rare candidates (band shell, periodic self images in
-// half mode, the zero-shift self pair).
-template <typename T>
-__device__ __forceinline__ bool rare_decision(const SearchArgs<T>& args,
-                                              const StructurePlan<T>& plan, int32_t source,
-                                              int32_t slot, int32_t self, int32_t target,
-                                              bool exact, const long long (&ws)[3]) {
-    if (slot == self) return args.include_self != 0;
-    if (args.half_list && target < source) return false;
-    const int4 meta = args.ghost_meta[slot];
-    const long long shift[3] = {meta.x + ws[0], meta.y + ws[1], meta.z + ws[2]};
-    if (args.half_list && target == source && !canonical_shift(shift)) return false;
-    if (!exact) return true;
-    T vec[3];
-    exact_displacement(args.positions, source, target, shift, plan.cell, vec);
-    return exact_norm2(vec[0], vec[1], vec[2]) < plan.cutoff_squared;
-}
 
 // Per bin: bitmask words of all its sources (sources * ceil(candidates / 32)).
 template <typename T>
@@ -490,6 +473,8 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
     __shared__ StencilRows stencil[kSearchWarps];
     __shared__ V tile[kSearchWarps][32];
     __shared__ int32_t tile_slot[kSearchWarps][32];
+    __shared__ int4 tile_meta[kSearchWarps][32];
+    __shared__ V tile_orig[kSearchWarps][32];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -529,6 +514,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
             qs.x = qs.y = qs.z = qs.w = static_cast<T>(NAN);
             int32_t self = -1;
             long long ws[3] = {0, 0, 0};
+            T ps[3] = {T(0), T(0), T(0)};
             if (active) {
                 source = args.source_list[first_source + rank];
                 qs = reinterpret_cast<const V*>(args.wrapped)[source];
@@ -536,7 +522,25 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 ws[0] = args.wraps[3 * source];
                 ws[1] = args.wraps[3 * source + 1];
                 ws[2] = args.wraps[3 * source + 2];
+                ps[0] = args.positions[3 * source];
+                ps[1] = args.positions[3 * source + 1];
+                ps[2] = args.positions[3 * source + 2];
             }
+            // Candidate index of the source's own zero image: its bit is set
+            // or cleared per include_self after each chunk instead of going
+            // through the exact test.
+            int32_t self_k = -1;
+            if (active) {
+#pragma unroll
+                for (int r = 0; r < 9; ++r) {
+                    const int32_t begin_r = rows.prefix[r] + rows.delta[r];
+                    const int32_t length_r = rows.prefix[r + 1] - rows.prefix[r];
+                    if (self >= begin_r && self < begin_r + length_r) {
+                        self_k = rows.prefix[r] + (self - begin_r);
+                    }
+                }
+            }
+            const bool self_mine = self_k >= 0 && ((self_k & 31) % groups) == my_group;
             uint32_t count = 0;
             for (int32_t w = 0; w < words; ++w) {
                 V record;
@@ -556,8 +560,12 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 my_tile[lane] = record;
                 my_slot[lane] = record_slot;
                 __syncwarp();
+                // bits: accepted without the exact test (inside the inner
+                // radius, and for half lists target > source); search_bits:
+                // every candidate that may be a pair.  Their difference is the
+                // rare set (band shell, half-list periodic self images).
                 uint32_t bits = 0;
-                uint32_t rare_bits = 0;
+                uint32_t search_bits = 0;
     #pragma unroll 4
                 for (int j = my_group; j < 32; j += groups) {
                     const V g = my_tile[j];
@@ -565,35 +573,51 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                     const T dy = g.y - qs.y;
                     const T dz = g.z - qs.z;
                     const T d2 = dx * dx + dy * dy + dz * dz;
-                    const bool inner = d2 < inner2;
-                    const int32_t target = lane_to_index(g.w);
-                    bool cheap = inner;
-                    bool rare = !inner && d2 < search2;
+                    bool in_inner = d2 < inner2;
+                    bool in_search = d2 < search2;
                     if constexpr (Half) {
-                        cheap = cheap && target > source;
-                        rare = rare || (inner && target == source);
-                    } else {
-                        // Full list: inner candidates with target == source (the
-                        // zero-shift self pair, periodic self images) are decided
-                        // exactly below.
-                        cheap = cheap && target != source;
-                        rare = rare || (inner && target == source);
+                        const int32_t order = lane_to_index(g.w) - source;
+                        in_inner = in_inner && order > 0;
+                        in_search = in_search && order >= 0;
                     }
-                    bits |= static_cast<uint32_t>(cheap) << j;
-                    rare_bits |= static_cast<uint32_t>(rare) << j;
+                    bits |= static_cast<uint32_t>(in_inner) << j;
+                    search_bits |= static_cast<uint32_t>(in_search) << j;
+                }
+                uint32_t rare_bits = search_bits & ~bits;
+                if (self_mine && (self_k >> 5) == w) {
+                    const uint32_t bit = 1u << (self_k & 31);
+                    bits = args.include_self ? (bits | bit) : (bits & ~bit);
+                    rare_bits &= ~bit;
                 }
                 if (!active) rare_bits = 0;
-                while (rare_bits) {
-                    const int j = __ffs(rare_bits) - 1;
-                    rare_bits &= rare_bits - 1;
-                    const V g = my_tile[j];
-                    const T dx = g.x - qs.x;
-                    const T dy = g.y - qs.y;
-                    const T dz = g.z - qs.z;
-                    const bool exact = !((dx * dx + dy * dy + dz * dz) < inner2);
-                    if (rare_decision(args, plan, source, my_slot[j], self, lane_to_index(g.w),
-                                      exact, ws)) {
-                        bits |= 1u << j;
+                if (__any_sync(kFullMask, rare_bits != 0u)) {
+                    // Rare candidates in this chunk: stage the chunk's ghost
+                    // shifts and original target positions once, then decide
+                    // each rare candidate from shared memory.
+                    if (record_slot >= 0) {
+                        tile_meta[warp][lane] = args.ghost_meta[record_slot];
+                        tile_orig[warp][lane] = reinterpret_cast<const V*>(args.ghost_orig)[record_slot];
+                    }
+                    __syncwarp();
+                    while (rare_bits) {
+                        const int j = __ffs(rare_bits) - 1;
+                        rare_bits &= rare_bits - 1;
+                        const V g = my_tile[j];
+                        const int4 meta = tile_meta[warp][j];
+                        const long long shift[3] = {meta.x + ws[0], meta.y + ws[1], meta.z + ws[2]};
+                        bool keep = true;
+                        if (Half && meta.w == source) keep = canonical_shift(shift);
+                        const T dx = g.x - qs.x;
+                        const T dy = g.y - qs.y;
+                        const T dz = g.z - qs.z;
+                        if (keep && !((dx * dx + dy * dy + dz * dz) < inner2)) {
+                            const V pt = tile_orig[warp][j];
+                            const T vx = exact_component(pt.x, ps[0], shift, plan.cell, 0);
+                            const T vy = exact_component(pt.y, ps[1], shift, plan.cell, 1);
+                            const T vz = exact_component(pt.z, ps[2], shift, plan.cell, 2);
+                            keep = exact_norm2(vx, vy, vz) < plan.cutoff_squared;
+                        }
+                        if (keep) bits |= 1u << j;
                     }
                 }
                 for (int offset = static_cast<int>(width); offset < 32; offset <<= 1) {
