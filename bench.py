@@ -51,6 +51,8 @@ def parse_args():
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", default="cfg5")
+    parser.add_argument("--size", type=int, default=None,
+                        help="reduced size for profiling: atoms (cfg4) or structures (cfg2/3/5)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--extra", default="cfg4",
@@ -68,16 +70,21 @@ def peak_hbm():
 SEEDS = {"cfg1": 0, "cfg2": 2, "cfg3": 3, "cfg4": 4, "cfg5": 5}
 
 
-def make_workload(name: str, rank: int, world: int = 1):
+SIZE_KEYWORD = {"cfg2": "n_structures", "cfg3": "n_structures", "cfg4": "n_atoms",
+                "cfg5": "n_structures"}
+
+
+def make_workload(name: str, rank: int, world: int = 1, size: int | None = None):
     """The rank's share of the job.  N=1: the configuration itself.  N>1
     (weak scaling): the global batch is N seeded copies of the configuration
     (seeds s, s+1, ...), split into N contiguous shards balanced by estimated
     pair count (tonari_b200.sharding); a single structure is never split."""
     from tonari_b200 import sharding, workloads
 
+    extra = {SIZE_KEYWORD[name]: size} if size else {}
     if world == 1:
-        return workloads.CONFIGS[name](seed=SEEDS[name])
-    parts = [workloads.CONFIGS[name](seed=SEEDS[name] + k) for k in range(world)]
+        return workloads.CONFIGS[name](seed=SEEDS[name], **extra)
+    parts = [workloads.CONFIGS[name](seed=SEEDS[name] + k, **extra) for k in range(world)]
     whole = workloads.concatenate(parts, f"{name}x{world}")
     weights = sharding.estimate_pairs(whole.batch_ptr, whole.cell, whole.pbc, whole.cutoff,
                                       half_list=whole.options.get("half_list", False))
@@ -255,17 +262,33 @@ def cpu_reference_rate(w, max_seconds=3.0):
             "structures_per_s": count / seconds}
 
 
+def measured_traffic_per_pair():
+    """Write-kernel DRAM bytes per emitted pair from the committed ncu summary
+    (profiles/traffic_cfg5_1024.md), or None."""
+    path = ROOT / "profiles" / "traffic_cfg5_1024.md"
+    if path.exists():
+        for line in path.read_text().splitlines():
+            if line.startswith("write_kernel_traffic_bytes_per_pair:"):
+                return float(line.split(":")[1])
+    return None
+
+
 def roofline(w, n_pairs, write_ms, step_ms):
     from tonari_b200.workloads import algorithmic_bytes
 
     peak, source = peak_hbm()
     traffic_bytes = algorithmic_bytes(w, n_pairs)
     achieved = traffic_bytes / (write_ms * 1e-3) / 1e9
+    per_pair = measured_traffic_per_pair() if w.name.startswith("cfg5") else None
+    traffic = int(per_pair * n_pairs) if per_pair else None
+    traffic_source = ("ncu dram read+write of cell_write_kernel on cfg5[:1024], scaled by pairs "
+                      "(profiles/traffic_cfg5_1024.md)" if traffic else None)
     call = traffic_bytes / (step_ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": f"{source} hbm_gbs",
             "kernel": "cell/brute write pass", "algorithmic_bytes": traffic_bytes,
-            "traffic": None, "call_achieved": round(call, 1), "call_frac": round(call / peak, 4)}
+            "traffic": traffic, "traffic_source": traffic_source,
+            "call_achieved": round(call, 1), "call_frac": round(call / peak, 4)}
 
 
 def run_reference(args):
@@ -275,7 +298,7 @@ def run_reference(args):
         return
     from oracle import oracle
 
-    w = make_workload(args.workload, 0)
+    w = make_workload(args.workload, 0, 1, args.size)
     rates, samples = [], None
     for step in range(args.warmup + args.steps):
         result = cpu_reference_rate(w, max_seconds=1.0)
@@ -319,7 +342,7 @@ def main():
 
     load_torch_cuda()
 
-    w = make_workload(args.workload, rank, world)
+    w = make_workload(args.workload, rank, world, args.size)
 
     def barrier():
         if world > 1:
