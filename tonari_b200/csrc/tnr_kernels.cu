@@ -648,6 +648,16 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
 // Unsorted calls write pairs in cell order, so one bin is one contiguous
 // output range and the queue streams across its sources; sorted calls write
 // each source's pairs at its own offset and flush at source boundaries.
+// Distance of an emitted pair from its displacement.  float: d2 * rsqrt(d2)
+// (relative error ~2^-22, far inside the 1e-5 contract); double: sqrt.
+__device__ __forceinline__ float pair_distance(float x, float y, float z) {
+    const float d2 = exact_norm2(x, y, z);
+    return d2 > 0.0f ? d2 * rsqrtf(d2) : 0.0f;
+}
+__device__ __forceinline__ double pair_distance(double x, double y, double z) {
+    return sqrt(exact_norm2(x, y, z));
+}
+
 template <typename T>
 struct WriteShared {
     int32_t queue_k[64];
@@ -658,7 +668,17 @@ struct WriteShared {
     T stage_D[96];
 };
 
-template <typename T>
+// Output sets the write kernels are specialised for (tnr_quantity bits);
+// any other set uses the run-time checked variant (Q = 0).
+constexpr int kQ_I = 1, kQ_J = 2, kQ_P = 4, kQ_S = 8, kQ_d = 16, kQ_D = 32;
+
+template <int Q>
+__device__ __forceinline__ bool wants(const void* pointer, int bit) {
+    if constexpr (Q == 0) return pointer != nullptr;
+    return (Q & bit) != 0;
+}
+
+template <typename T, int Q>
 __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const StructurePlan<T>& plan,
                                             const StencilRows& rows, WriteShared<T>& sh,
                                             int32_t n, int64_t out_row, int lane,
@@ -697,19 +717,18 @@ __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const Str
         } else {
             target = lane_to_index(reinterpret_cast<const V*>(args.ghost_pos)[slot].w);
         }
-        const int64_t o = out_row + lane;
         const int64_t s = source + args.index_offset;
         const int64_t t = target + args.index_offset;
-        if (args.out_i) args.out_i[o] = s;
-        if (args.out_j) args.out_j[o] = t;
-        if (args.out_P) reinterpret_cast<longlong2*>(args.out_P)[o] = make_longlong2(s, t);
-        if (args.out_d) args.out_d[o] = sqrt(exact_norm2(vec[0], vec[1], vec[2]));
-        if (args.out_S) {
+        if (wants<Q>(args.out_i, kQ_I)) (args.out_i + out_row)[lane] = s;
+        if (wants<Q>(args.out_j, kQ_J)) (args.out_j + out_row)[lane] = t;
+        if (wants<Q>(args.out_P, kQ_P)) (reinterpret_cast<longlong2*>(args.out_P) + out_row)[lane] = make_longlong2(s, t);
+        if (wants<Q>(args.out_d, kQ_d)) (args.out_d + out_row)[lane] = pair_distance(vec[0], vec[1], vec[2]);
+        if (wants<Q>(args.out_S, kQ_S)) {
             sh.stage_S[3 * lane] = shift[0];
             sh.stage_S[3 * lane + 1] = shift[1];
             sh.stage_S[3 * lane + 2] = shift[2];
         }
-        if (args.out_D) {
+        if (wants<Q>(args.out_D, kQ_D)) {
             sh.stage_D[3 * lane] = vec[0];
             sh.stage_D[3 * lane + 1] = vec[1];
             sh.stage_D[3 * lane + 2] = vec[2];
@@ -717,7 +736,7 @@ __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const Str
     }
     __syncwarp();
     const int32_t words = 3 * n;
-    if (args.out_S) {
+    if (wants<Q>(args.out_S, kQ_S)) {
         int32_t* out = args.out_S + 3 * out_row;
 #pragma unroll
         for (int m = 0; m < 3; ++m) {
@@ -725,7 +744,7 @@ __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const Str
             if (e < words) out[e] = sh.stage_S[e];
         }
     }
-    if (args.out_D) {
+    if (wants<Q>(args.out_D, kQ_D)) {
         T* out = args.out_D + 3 * out_row;
 #pragma unroll
         for (int m = 0; m < 3; ++m) {
@@ -736,15 +755,15 @@ __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const Str
     __syncwarp();
 }
 
-template <typename T>
+template <typename T, int Q>
 __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
     __shared__ StencilRows stencil[kSearchWarps];
     __shared__ WriteShared<T> shared[kSearchWarps];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const bool need_vector = args.out_d != nullptr || args.out_D != nullptr;
-    const bool need_shift = args.out_S != nullptr;
+    const bool need_vector = wants<Q>(args.out_d, kQ_d) || wants<Q>(args.out_D, kQ_D);
+    const bool need_shift = wants<Q>(args.out_S, kQ_S);
     const bool by_atom = args.source_order == 0;
     WriteShared<T>& sh = shared[warp];
     const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -821,7 +840,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
                             sh.queue_k[lane] = slot_of(rows, 32 * item_w + bit);
                             sh.queue_r[lane] = static_cast<uint8_t>(item_r);
                         }
-                        flush_queue(args, plan, rows, sh, n, out_row + i, lane, need_shift,
+                        flush_queue<T, Q>(args, plan, rows, sh, n, out_row + i, lane, need_shift,
                                     need_vector);
                     }
                     out_row += produced;
@@ -1087,8 +1106,20 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
     if (args.n_sources == 0 || args.n_bins == 0) return;
     const int64_t needed = blocks_for(args.n_bins, kSearchWarps);
     if (write) {
-        cell_write_kernel<T><<<persistent_blocks(cell_write_kernel<T>, kSearchThreads, needed),
-                               kSearchThreads, 0, stream>>>(args);
+        const int q = (args.out_i ? kQ_I : 0) | (args.out_j ? kQ_J : 0) | (args.out_P ? kQ_P : 0) |
+                      (args.out_S ? kQ_S : 0) | (args.out_d ? kQ_d : 0) | (args.out_D ? kQ_D : 0);
+        auto launch = [&](auto kernel) {
+            kernel<<<persistent_blocks(kernel, kSearchThreads, needed), kSearchThreads, 0, stream>>>(
+                args);
+        };
+        switch (q) {
+            case kQ_P | kQ_S: launch(cell_write_kernel<T, kQ_P | kQ_S>); break;
+            case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
+                launch(cell_write_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>); break;
+            case kQ_P | kQ_S | kQ_D: launch(cell_write_kernel<T, kQ_P | kQ_S | kQ_D>); break;
+            case kQ_P | kQ_D: launch(cell_write_kernel<T, kQ_P | kQ_D>); break;
+            default: launch(cell_write_kernel<T, 0>); break;
+        }
     } else if (args.half_list) {
         cell_count_kernel<T, true><<<persistent_blocks(cell_count_kernel<T, true>, kSearchThreads,
                                                        needed), kSearchThreads, 0, stream>>>(args);
