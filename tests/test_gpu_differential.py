@@ -199,3 +199,25 @@ def test_sorted_and_unsorted_orders_hold_the_same_pairs(half_list):
     assert_same_pairs(unsorted[0], unsorted[1], ordered[0], ordered[1])
     a = canonical(unsorted[0], unsorted[1])
     assert len(a) > 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+def test_fused_displacement_gradients_match_reference_formula(dtype):
+    # The backward of the fused d/D equals autograd through the reference
+    # formula (src/tonari/_torch_frontend.py:94-104) on the same pairs.
+    positions, cell, pbc, batch_ptr = periodic_batch(dtype)
+    pos_a = positions.cuda().requires_grad_()
+    cell_a = cell.cuda().requires_grad_()
+    d, D, pairs, shifts = neighbor_list("dDPS", pos_a, cell_a, pbc.cuda(), 1.2, batch_ptr.cuda())
+    weights = torch.linspace(0.5, 1.5, len(d), device="cuda", dtype=dtype)
+    ((weights * d).sum() + (D ** 2).sum()).backward()
+    pos_b = positions.cuda().requires_grad_()
+    cell_b = cell.cuda().requires_grad_()
+    pair_batch = torch.bucketize(pairs[:, 0].contiguous(), batch_ptr.cuda()[1:], right=True)
+    D_ref = pos_b[pairs[:, 1]] - pos_b[pairs[:, 0]] + torch.einsum(
+        "ei,eij->ej", shifts.to(dtype), cell_b[pair_batch])
+    d_ref = torch.linalg.vector_norm(D_ref, dim=1)
+    ((weights * d_ref).sum() + (D_ref ** 2).sum()).backward()
+    tol = 1e-4 if dtype == torch.float32 else 1e-10
+    torch.testing.assert_close(pos_a.grad, pos_b.grad, rtol=tol, atol=tol)
+    torch.testing.assert_close(cell_a.grad, cell_b.grad, rtol=tol, atol=tol)

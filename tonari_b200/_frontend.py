@@ -5,8 +5,9 @@ Normalisation and validation restate tonari src/tonari/_torch_frontend.py:25-75
 kernel for every requested quantity at once (i/j/P/S/d/D fused into the write
 pass) instead of assembling i/j/d/D with extra passes
 (src/tonari/_torch_frontend.py:78-105).  When autograd needs gradients of d/D
-with respect to positions or cell, d/D are computed with the reference's own
-formula from the kernel's P/S, so the gradient contract is unchanged.
+with respect to positions or cell, the kernel's D enters a custom autograd
+function whose backward is the analytic gradient of the reference formula, so
+the gradient contract is unchanged.
 """
 from __future__ import annotations
 
@@ -78,6 +79,34 @@ def public_displacements(positions: Tensor, cell: Tensor, batch_ptr: Tensor,
     )
 
 
+class _KernelDisplacements(torch.autograd.Function):
+    """D from the kernel in the forward; the analytic gradient of the
+    reference formula D = pos[j] - pos[i] + S @ cell[b(i)]
+    (src/tonari/_torch_frontend.py:94-104) in the backward:
+    dL/dpos[j] += g, dL/dpos[i] -= g, dL/dcell[b] += S^T g."""
+
+    @staticmethod
+    def forward(ctx, positions, cell, displacements, source, target, shifts, pair_batch):
+        ctx.save_for_backward(source, target, shifts, pair_batch)
+        ctx.shapes = (positions.shape, cell.shape)
+        return displacements
+
+    @staticmethod
+    def backward(ctx, grad):
+        source, target, shifts, pair_batch = ctx.saved_tensors
+        positions_shape, cell_shape = ctx.shapes
+        grad_positions = grad_cell = None
+        if ctx.needs_input_grad[0]:
+            grad_positions = grad.new_zeros(positions_shape)
+            grad_positions.index_add_(0, target, grad)
+            grad_positions.index_add_(0, source, -grad)
+        if ctx.needs_input_grad[1]:
+            grad_cell = grad.new_zeros(cell_shape)
+            outer = shifts.to(grad.dtype).unsqueeze(2) * grad.unsqueeze(1)  # (E, 3, 3)
+            grad_cell.index_add_(0, pair_batch, outer)
+        return grad_positions, grad_cell, None, None, None, None, None
+
+
 def neighbor_list_torch(quantities, positions, cell, pbc, cutoff, batch_ptr, *, algorithm,
                         cpu_threads, sorted, half_list, include_self, index_offset=0):
     _require_torch_tensors(cell=cell, pbc=pbc, batch_ptr=batch_ptr)
@@ -102,7 +131,7 @@ def neighbor_list_torch(quantities, positions, cell, pbc, cutoff, batch_ptr, *, 
     )
     requested = set(quantities)
     if differentiable:
-        requested = (requested - {"d", "D"}) | {"P", "S"}
+        requested |= {"P", "S", "D"}
     values = backend.neighbor_list_fused(
         positions.detach().contiguous(), batch_ptr.contiguous(), cell.detach().contiguous(),
         pbc.contiguous(), cutoff, half_list, include_self, algorithm, sorted,
@@ -112,7 +141,11 @@ def neighbor_list_torch(quantities, positions, cell, pbc, cutoff, batch_ptr, *, 
         pairs = values["P"]
         if index_offset:
             pairs = pairs - index_offset
-        displacements = public_displacements(positions, cell, batch_ptr, pairs, values["S"])
+        source = pairs[:, 0].contiguous()
+        target = pairs[:, 1].contiguous()
+        pair_batch = torch.bucketize(source, batch_ptr[1:], right=True)
+        displacements = _KernelDisplacements.apply(
+            positions, cell, values["D"], source, target, values["S"], pair_batch)
         values["D"] = displacements
         if "d" in quantities:
             values["d"] = torch.linalg.vector_norm(displacements, dim=1)

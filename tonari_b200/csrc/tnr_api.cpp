@@ -66,10 +66,7 @@ void check_cuda(cudaError_t error, const char* what) {
     }
 }
 
-void check_launch(const char* what) {
-    ++g_launches;
-    check_cuda(cudaGetLastError(), what);
-}
+void check_launch(const char* what) { check_cuda(cudaGetLastError(), what); }
 
 // ---- allocation ------------------------------------------------------------
 
@@ -757,6 +754,7 @@ int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator
     }
     *result = tnr_result{};
     g_launches = 0;
+    const int64_t launches_before = launched_kernels();
     tnr_allocator chosen{nullptr, default_allocate, default_release};
     if (allocator && allocator->allocate && allocator->release) chosen = *allocator;
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_handle);
@@ -780,6 +778,7 @@ int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator
         }
         workspace.keep_outputs();
         *result = local;
+        g_launches = launched_kernels() - launches_before;
         return TNR_OK;
     } catch (const InputError& error) {
         workspace.release_outputs();

@@ -1058,11 +1058,18 @@ unsigned persistent_blocks(Kernel kernel, int threads, int64_t needed) {
 // ---------------------------------------------------------------------------
 namespace tnr {
 
+namespace {
+thread_local int64_t g_kernel_launches = 0;
+}  // namespace
+
+int64_t launched_kernels() { return g_kernel_launches; }
+
 template <typename T>
 void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream) {
     if (args.n_atoms == 0) return;
     prepare_kernel<T><<<static_cast<unsigned>(blocks_for(args.n_atoms, kPrepareThreads)),
                         kPrepareThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
 }
 
 template <typename T>
@@ -1071,8 +1078,10 @@ void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream) {
     const unsigned blocks = static_cast<unsigned>(blocks_for(args.n_cell_atoms, kBinThreads));
     if (scatter) {
         bin_kernel<T, true><<<blocks, kBinThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     } else {
         bin_kernel<T, false><<<blocks, kBinThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     }
 }
 
@@ -1082,6 +1091,7 @@ void launch_image_table(const StructurePlan<T>* plans, int64_t batch, int4* shif
     if (batch == 0) return;
     image_table_kernel<T><<<static_cast<unsigned>(batch), 128, 0, stream>>>(plans, shifts,
                                                                           translations);
+    ++g_kernel_launches;
 }
 
 template <typename T>
@@ -1090,6 +1100,7 @@ void launch_bin_struct(const int64_t* cell_bin_prefix, const int32_t* cell_struc
     if (n_cell == 0) return;
     bin_struct_kernel<<<static_cast<unsigned>(n_cell), 256, 0, stream>>>(cell_bin_prefix,
                                                                         cell_structs, bin_struct);
+    ++g_kernel_launches;
 }
 
 template <typename T>
@@ -1099,6 +1110,7 @@ void launch_stencil_words(const SearchArgs<T>& args, unsigned long long* bin_wor
     const unsigned blocks = persistent_blocks(stencil_words_kernel<T>, kBinThreads,
                                               blocks_for(args.n_bins, kBinThreads / 32));
     stencil_words_kernel<T><<<blocks, kBinThreads, 0, stream>>>(args, args.n_bins, bin_words);
+    ++g_kernel_launches;
 }
 
 template <typename T>
@@ -1111,6 +1123,7 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
         auto launch = [&](auto kernel) {
             kernel<<<persistent_blocks(kernel, kSearchThreads, needed), kSearchThreads, 0, stream>>>(
                 args);
+    ++g_kernel_launches;
         };
         switch (q) {
             case kQ_P | kQ_S: launch(cell_write_kernel<T, kQ_P | kQ_S>); break;
@@ -1123,9 +1136,11 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
     } else if (args.half_list) {
         cell_count_kernel<T, true><<<persistent_blocks(cell_count_kernel<T, true>, kSearchThreads,
                                                        needed), kSearchThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     } else {
         cell_count_kernel<T, false><<<persistent_blocks(cell_count_kernel<T, false>, kSearchThreads,
                                                         needed), kSearchThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     }
 }
 
@@ -1137,10 +1152,12 @@ void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t str
         brute_search_kernel<T, true><<<persistent_blocks(brute_search_kernel<T, true>,
                                                          kSearchThreads, needed),
                                        kSearchThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     } else {
         brute_search_kernel<T, false><<<persistent_blocks(brute_search_kernel<T, false>,
                                                           kSearchThreads, needed),
                                         kSearchThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     }
 }
 
@@ -1168,6 +1185,7 @@ void launch_scan(const In* in, int64_t n, Out* out, Out* out2, void* workspace,
     state.inclusive = state.aggregate + tiles;
     exclusive_scan_kernel<In, Out><<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
         in, n, out, out2, state, status);
+    ++g_kernel_launches;
 }
 }  // namespace
 

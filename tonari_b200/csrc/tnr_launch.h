@@ -113,6 +113,9 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
 template <typename T>
 void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t stream);
 
+// Running count of kernels this host thread has launched through this file.
+int64_t launched_kernels();
+
 // Exclusive scans (n+1 outputs).  `tile_words` is workspace of
 // scan_workspace_bytes(n) bytes; it is cleared inside.
 size_t scan_workspace_bytes(int64_t n);
