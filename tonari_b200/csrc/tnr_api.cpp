@@ -554,6 +554,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     int4* d_ghost_meta = nullptr;
     int32_t* d_self_slot = nullptr;
     int32_t* d_source_list = nullptr;
+    int32_t* d_source_bin = nullptr;
     uint32_t* d_mask_words = nullptr;
     unsigned long long* d_bin_word_start = nullptr;
     const int64_t scan_items = std::max<int64_t>(n_atoms, total_bins);
@@ -629,6 +630,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         d_ghost_orig = workspace.get<V4>(ghosts);
         d_self_slot = workspace.get<int32_t>(n_atoms);
         d_source_list = workspace.get<int32_t>(n_cell_atoms);
+        d_source_bin = workspace.get<int32_t>(n_cell_atoms);
         bin_args.bin_counts = d_cursor;
         bin_args.ghost_pos = d_ghost_pos;
         bin_args.ghost_meta = d_ghost_meta;
@@ -636,6 +638,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         bin_args.positions = static_cast<const T*>(request.positions);
         bin_args.self_slot = d_self_slot;
         bin_args.source_list = d_source_list;
+        bin_args.source_bin = d_source_bin;
         launch_bin(bin_args, true, stream);
         check_launch("bin scatter kernel");
     }
@@ -656,6 +659,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.ghost_meta = d_ghost_meta;
     search.self_slot = d_self_slot;
     search.source_list = d_source_list;
+    search.source_bin = d_source_bin;
     search.n_sources = n_cell_atoms;
     search.image_shift = bin_args.image_shift;
     search.mask_words = d_mask_words;

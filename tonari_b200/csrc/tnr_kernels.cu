@@ -287,6 +287,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
                                               image.z - wrap[2], static_cast<int32_t>(atom));
             if (k == center) {
                 args.source_list[static_cast<uint32_t>(old >> 32)] = static_cast<int32_t>(atom);
+                args.source_bin[static_cast<uint32_t>(old >> 32)] = static_cast<int32_t>(bin);
                 args.self_slot[atom] = static_cast<int32_t>(slot);
             }
         }
@@ -467,6 +468,61 @@ __global__ void __launch_bounds__(kBinThreads) stencil_words_kernel(SearchArgs<T
 // per-lane bit word and decided after the chunk.  Accepted-candidate bits are
 // stored transposed -- word w of source rank r at base + w * S + r, S the
 // bin's source count -- so each chunk's store is coalesced.
+// Spreads the low 32/G bits of x to positions 0, G, 2G, ... (G a power of
+// two), by successive doubling of the gaps.
+template <int G>
+__device__ __forceinline__ uint32_t spread_bits(uint32_t x) {
+    if constexpr (G == 1) {
+        return x;
+    } else {
+        // Each step doubles the distance between the remaining bit groups.
+        uint32_t y = x;
+        if constexpr (G >= 2) {
+            y = (y | (y << 8)) & 0x00ff00ffu;
+            y = (y | (y << 4)) & 0x0f0f0f0fu;
+            y = (y | (y << 2)) & 0x33333333u;
+            y = (y | (y << 1)) & 0x55555555u;  // 16 bits -> even positions
+        }
+        if constexpr (G >= 4) {
+            // 8 bits now sit at even positions 0..14; spread them to 0, 4, ..., 28.
+            uint32_t z = 0;
+#pragma unroll
+            for (int b = 0; b < 32 / G; ++b) z |= ((y >> (2 * b)) & 1u) << (G * b);
+            y = z;
+        }
+        return y;
+    }
+}
+
+// Tests one 32-candidate tile against this lane's source.  With G lane groups
+// the lane takes candidates j = my_group + G * jj; the bits are accumulated
+// compactly (bit jj) with compile-time shifts and spread once at the end.
+template <typename T, bool Half, int G>
+__device__ __forceinline__ void test_tile(const vec4_t<T>* tile, const vec4_t<T>& qs,
+                                          int32_t source, T inner2, T search2, int my_group,
+                                          uint32_t& bits, uint32_t& search_bits) {
+    uint32_t inner_compact = 0, search_compact = 0;
+#pragma unroll
+    for (int jj = 0; jj < 32 / G; ++jj) {
+        const vec4_t<T> g = tile[my_group + G * jj];
+        const T dx = g.x - qs.x;
+        const T dy = g.y - qs.y;
+        const T dz = g.z - qs.z;
+        const T d2 = dx * dx + dy * dy + dz * dz;
+        bool in_inner = d2 < inner2;
+        bool in_search = d2 < search2;
+        if constexpr (Half) {
+            const int32_t order = lane_to_index(g.w) - source;
+            in_inner = in_inner && order > 0;
+            in_search = in_search && order >= 0;
+        }
+        inner_compact |= static_cast<uint32_t>(in_inner) << jj;
+        search_compact |= static_cast<uint32_t>(in_search) << jj;
+    }
+    bits = spread_bits<G>(inner_compact) << my_group;
+    search_bits = spread_bits<G>(search_compact) << my_group;
+}
+
 template <typename T, bool Half>
 __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
@@ -542,46 +598,45 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
             }
             const bool self_mine = self_k >= 0 && ((self_k & 31) % groups) == my_group;
             uint32_t count = 0;
-            for (int32_t w = 0; w < words; ++w) {
-                V record;
-                int32_t record_slot = -1;
-                const int32_t k = 32 * w + lane;
+            // Per-lane cursor over the concatenated stencil rows: candidate k
+            // = 32 w + lane lives in row `row` at slot k + delta[row]; the row
+            // advances by at most a few steps per chunk.  The next chunk's
+            // record is loaded while the current tile is tested.
+            int32_t row = 0;
+            auto record_of = [&](int32_t k, int32_t& slot_out) {
+                V rec;
                 if (k < total) {
-                    const int32_t slot = slot_of(rows, k);
-                    record = reinterpret_cast<const V*>(args.ghost_pos)[slot];
-                    record_slot = slot;
+                    while (rows.prefix[row + 1] <= k) ++row;
+                    slot_out = k + rows.delta[row];
+                    rec = reinterpret_cast<const V*>(args.ghost_pos)[slot_out];
                 } else {
-                    record.x = static_cast<T>(INFINITY);
-                    record.y = T(0);
-                    record.z = T(0);
-                    record.w = index_to_lane(-1, T(0));
+                    slot_out = -1;
+                    rec.x = static_cast<T>(INFINITY);
+                    rec.y = T(0);
+                    rec.z = T(0);
+                    rec.w = index_to_lane(-1, T(0));
                 }
+                return rec;
+            };
+            int32_t next_slot = -1;
+            V next_record = record_of(lane, next_slot);
+            for (int32_t w = 0; w < words; ++w) {
+                const V record = next_record;
+                const int32_t record_slot = next_slot;
+                if (w + 1 < words) next_record = record_of(32 * (w + 1) + lane, next_slot);
                 __syncwarp();
                 my_tile[lane] = record;
                 my_slot[lane] = record_slot;
                 __syncwarp();
-                // bits: accepted without the exact test (inside the inner
-                // radius, and for half lists target > source); search_bits:
-                // every candidate that may be a pair.  Their difference is the
-                // rare set (band shell, half-list periodic self images).
                 uint32_t bits = 0;
                 uint32_t search_bits = 0;
-    #pragma unroll 4
-                for (int j = my_group; j < 32; j += groups) {
-                    const V g = my_tile[j];
-                    const T dx = g.x - qs.x;
-                    const T dy = g.y - qs.y;
-                    const T dz = g.z - qs.z;
-                    const T d2 = dx * dx + dy * dy + dz * dz;
-                    bool in_inner = d2 < inner2;
-                    bool in_search = d2 < search2;
-                    if constexpr (Half) {
-                        const int32_t order = lane_to_index(g.w) - source;
-                        in_inner = in_inner && order > 0;
-                        in_search = in_search && order >= 0;
-                    }
-                    bits |= static_cast<uint32_t>(in_inner) << j;
-                    search_bits |= static_cast<uint32_t>(in_search) << j;
+                switch (groups) {
+                    case 1: test_tile<T, Half, 1>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
+                    case 2: test_tile<T, Half, 2>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
+                    case 4: test_tile<T, Half, 4>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
+                    case 8: test_tile<T, Half, 8>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
+                    case 16: test_tile<T, Half, 16>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
+                    default: test_tile<T, Half, 32>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
                 }
                 uint32_t rare_bits = search_bits & ~bits;
                 if (self_mine && (self_k >> 5) == w) {
@@ -844,6 +899,158 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
                                     need_vector);
                     }
                     out_row += produced;
+                }
+            }
+        }
+    }
+}
+
+// Write pass for unsorted calls.  In cell order any 32 consecutive sources
+// own one contiguous output range, whatever bins they belong to, so one warp
+// takes 32 consecutive sources, one per lane, each with its own stencil-row
+// table.  In every round each lane that still has pairs takes its next
+// accepted candidate from its bitmask words and emits one pair; the round's
+// rows are assigned by a ballot prefix, so each store instruction covers one
+// contiguous run of rows.
+template <typename T, int Q>
+__global__ void __launch_bounds__(kSearchThreads) cell_emit_kernel(SearchArgs<T> args) {
+    using V = vec4_t<T>;
+    __shared__ StencilRows lane_rows[kSearchWarps][32];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned below = (1u << lane) - 1u;
+    const bool need_vector = wants<Q>(args.out_d, kQ_d) || wants<Q>(args.out_D, kQ_D);
+    const bool need_shift = wants<Q>(args.out_S, kQ_S) || need_vector;
+    const int64_t n_groups = (args.n_sources + 31) / 32;
+    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t group = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         group < n_groups; group += stride) {
+        const int64_t k = group * 32 + lane;
+        const bool valid = k < args.n_sources;
+        int32_t remaining = 0;
+        int32_t source = 0, words = 0, word_index = -1;
+        uint32_t word = 0;
+        const uint32_t* mask = nullptr;
+        int64_t mask_stride = 0;
+        const StructurePlan<T>* plan = nullptr;
+        T ps[3] = {T(0), T(0), T(0)};
+        int32_t ws[3] = {0, 0, 0};
+        StencilRows& rows = lane_rows[warp][lane];
+        if (valid) {
+            source = args.source_list[k];
+            remaining = static_cast<int32_t>(args.counts[k]);
+            const int32_t bin = args.source_bin[k];
+            const uint32_t first = static_cast<uint32_t>(args.bin_start[bin] >> 32);
+            const uint32_t n_bin_sources = static_cast<uint32_t>(args.bin_start[bin + 1] >> 32) - first;
+            plan = &args.plans[args.bin_struct[bin]];
+            int32_t bx, by, bz;
+            bin_coordinates(*plan, bin, bx, by, bz);
+            // This lane's stencil rows and prefix table.
+            int32_t prefix = 0;
+#pragma unroll
+            for (int r = 0; r < 9; ++r) {
+                int32_t begin = 0, length = 0;
+                const int32_t x = bx + r / 3 - 1;
+                const int32_t y = by + r % 3 - 1;
+                if (x >= 0 && x < plan->dims[0] && y >= 0 && y < plan->dims[1]) {
+                    const int32_t z0 = max(bz - 1, 0);
+                    const int32_t z1 = min(bz + 1, plan->dims[2] - 1);
+                    const int64_t row = plan->bin_begin +
+                        (static_cast<int64_t>(x) * plan->dims[1] + y) * plan->dims[2];
+                    begin = static_cast<int32_t>(args.bin_start[row + z0] & 0xffffffffull);
+                    length = static_cast<int32_t>(args.bin_start[row + z1 + 1] & 0xffffffffull) - begin;
+                }
+                rows.prefix[r] = prefix;
+                rows.delta[r] = begin - prefix;
+                prefix += length;
+            }
+            rows.prefix[9] = prefix;
+#pragma unroll
+            for (int r = 10; r < 16; ++r) rows.prefix[r] = INT_MAX;
+            words = (prefix + 31) >> 5;
+            mask = args.mask_words + args.bin_word_start[bin] + (k - first);
+            mask_stride = n_bin_sources;
+            ps[0] = args.positions[3 * source];
+            ps[1] = args.positions[3 * source + 1];
+            ps[2] = args.positions[3 * source + 2];
+            ws[0] = args.wraps[3 * source];
+            ws[1] = args.wraps[3 * source + 1];
+            ws[2] = args.wraps[3 * source + 2];
+        }
+        int64_t out_row = args.pair_start[min(group * 32, args.n_sources - 1)];
+        // Next accepted candidate of this lane (bitmask walk).
+        auto next_slot = [&]() -> int32_t {
+            while (word == 0u && word_index + 1 < words) {
+                ++word_index;
+                word = mask[static_cast<int64_t>(word_index) * mask_stride];
+            }
+            const int32_t bit = __ffs(word) - 1;
+            word &= word - 1u;
+            return slot_of(rows, 32 * word_index + bit);
+        };
+        // Software pipeline: the records of round r+1 are in flight while
+        // round r is computed and stored.
+        int4 meta = make_int4(0, 0, 0, 0);
+        V pt{};
+        if (remaining > 0) {
+            const int32_t slot = next_slot();
+            meta = args.ghost_meta[slot];
+            if (need_vector) pt = reinterpret_cast<const V*>(args.ghost_orig)[slot];
+        }
+        while (__any_sync(kFullMask, remaining > 0)) {
+            const bool active = remaining > 0;
+            const int4 cur_meta = meta;
+            const V cur_pt = pt;
+            if (remaining > 1) {
+                const int32_t slot = next_slot();
+                meta = args.ghost_meta[slot];
+                if (need_vector) pt = reinterpret_cast<const V*>(args.ghost_orig)[slot];
+            }
+            --remaining;
+            const unsigned ballot = __ballot_sync(kFullMask, active);
+            const int64_t o = out_row + __popc(ballot & below);
+            out_row += __popc(ballot);
+            if (active) {
+                const int64_t target = cur_meta.w;
+                int32_t shift[3] = {0, 0, 0};
+                T vec[3] = {T(0), T(0), T(0)};
+                if (need_shift) {
+                    // Cell-list shifts fit int32 by construction of the plan.
+                    shift[0] = cur_meta.x + ws[0];
+                    shift[1] = cur_meta.y + ws[1];
+                    shift[2] = cur_meta.z + ws[2];
+                }
+                if (need_vector) {
+                    const T s0 = static_cast<T>(shift[0]);
+                    const T s1 = static_cast<T>(shift[1]);
+                    const T s2 = static_cast<T>(shift[2]);
+                    const T* cell = plan->cell;
+                    vec[0] = add_rn(add_rn(add_rn(sub_rn(cur_pt.x, ps[0]), mul_rn(s0, cell[0])),
+                                           mul_rn(s1, cell[3])), mul_rn(s2, cell[6]));
+                    vec[1] = add_rn(add_rn(add_rn(sub_rn(cur_pt.y, ps[1]), mul_rn(s0, cell[1])),
+                                           mul_rn(s1, cell[4])), mul_rn(s2, cell[7]));
+                    vec[2] = add_rn(add_rn(add_rn(sub_rn(cur_pt.z, ps[2]), mul_rn(s0, cell[2])),
+                                           mul_rn(s1, cell[5])), mul_rn(s2, cell[8]));
+                }
+                const int64_t s = source + args.index_offset;
+                const int64_t t = target + args.index_offset;
+                if (wants<Q>(args.out_i, kQ_I)) args.out_i[o] = s;
+                if (wants<Q>(args.out_j, kQ_J)) args.out_j[o] = t;
+                if (wants<Q>(args.out_P, kQ_P)) {
+                    reinterpret_cast<longlong2*>(args.out_P)[o] = make_longlong2(s, t);
+                }
+                if (wants<Q>(args.out_S, kQ_S)) {
+                    int32_t* row = args.out_S + 3 * o;
+                    row[0] = shift[0];
+                    row[1] = shift[1];
+                    row[2] = shift[2];
+                }
+                if (wants<Q>(args.out_d, kQ_d)) args.out_d[o] = pair_distance(vec[0], vec[1], vec[2]);
+                if (wants<Q>(args.out_D, kQ_D)) {
+                    T* row = args.out_D + 3 * o;
+                    row[0] = vec[0];
+                    row[1] = vec[1];
+                    row[2] = vec[2];
                 }
             }
         }
@@ -1120,18 +1327,30 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
     if (write) {
         const int q = (args.out_i ? kQ_I : 0) | (args.out_j ? kQ_J : 0) | (args.out_P ? kQ_P : 0) |
                       (args.out_S ? kQ_S : 0) | (args.out_d ? kQ_d : 0) | (args.out_D ? kQ_D : 0);
-        auto launch = [&](auto kernel) {
-            kernel<<<persistent_blocks(kernel, kSearchThreads, needed), kSearchThreads, 0, stream>>>(
+        const int64_t groups = blocks_for((args.n_sources + 31) / 32, kSearchWarps);
+        auto launch = [&](auto kernel, int64_t work) {
+            kernel<<<persistent_blocks(kernel, kSearchThreads, work), kSearchThreads, 0, stream>>>(
                 args);
     ++g_kernel_launches;
         };
-        switch (q) {
-            case kQ_P | kQ_S: launch(cell_write_kernel<T, kQ_P | kQ_S>); break;
-            case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
-                launch(cell_write_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>); break;
-            case kQ_P | kQ_S | kQ_D: launch(cell_write_kernel<T, kQ_P | kQ_S | kQ_D>); break;
-            case kQ_P | kQ_D: launch(cell_write_kernel<T, kQ_P | kQ_D>); break;
-            default: launch(cell_write_kernel<T, 0>); break;
+        if (args.source_order == 0) {
+            switch (q) {
+                case kQ_P | kQ_S: launch(cell_write_kernel<T, kQ_P | kQ_S>, needed); break;
+                case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
+                    launch(cell_write_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>, needed); break;
+                case kQ_P | kQ_S | kQ_D: launch(cell_write_kernel<T, kQ_P | kQ_S | kQ_D>, needed); break;
+                case kQ_P | kQ_D: launch(cell_write_kernel<T, kQ_P | kQ_D>, needed); break;
+                default: launch(cell_write_kernel<T, 0>, needed); break;
+            }
+        } else {
+            switch (q) {
+                case kQ_P | kQ_S: launch(cell_emit_kernel<T, kQ_P | kQ_S>, groups); break;
+                case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
+                    launch(cell_emit_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>, groups); break;
+                case kQ_P | kQ_S | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_S | kQ_D>, groups); break;
+                case kQ_P | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_D>, groups); break;
+                default: launch(cell_emit_kernel<T, 0>, groups); break;
+            }
         }
     } else if (args.half_list) {
         cell_count_kernel<T, true><<<persistent_blocks(cell_count_kernel<T, true>, kSearchThreads,

@@ -38,6 +38,7 @@ struct BinArgs {
     const T* positions;
     int32_t* self_slot;          // [N]             (scatter only)
     int32_t* source_list;        // [sources]       (scatter only)
+    int32_t* source_bin;         // [sources]       (scatter only) bin of each listed source
     uint32_t* status;
     const int4* image_shift;        // [images] (x, y, z, 0), x-major per structure
     const void* image_translation;  // vec4_t<T> [images], shift . cell in T
@@ -56,6 +57,7 @@ struct SearchArgs {
     const int4* ghost_meta;
     const int32_t* self_slot;
     const int32_t* source_list;
+    const int32_t* source_bin;          // [sources] bin of each source, cell order
     int64_t n_sources;
     const int32_t* bin_struct;          // [bins] structure of each bin
     const void* ghost_orig;             // vec4_t<T> [G] original target position, target
