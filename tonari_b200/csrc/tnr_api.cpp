@@ -22,12 +22,14 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+
 #include <cstring>
 #include <limits>
 #include <string>
 #include <vector>
 
 #include "tnr_geometry.h"
+#include "tnr_pool.h"
 #include "tnr_launch.h"
 #include "tnr_plan.h"
 
@@ -502,11 +504,17 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         uint32_t status = 0;
         std::memcpy(&status, pinned_read + reductions.size() * sizeof(Reduction<T>), sizeof(status));
         check_status(status);
+        std::vector<CellPlan> outcomes(static_cast<size_t>(batch), CellPlan::kUnsafe);
+        HostPool::instance().parallel_for(batch, 256, [&](int64_t begin, int64_t end) {
+            for (int64_t b = begin; b < end; ++b) {
+                if (mode[b] != kModeCell) continue;
+                outcomes[b] = plan_cell(plans[b], reductions[b], cell_t.data() + 9 * b, request.cutoff);
+            }
+        });
         for (int64_t b = 0; b < batch; ++b) {
             if (mode[b] != kModeCell) continue;
             StructurePlan<T>& plan = plans[b];
-            const CellPlan outcome =
-                plan_cell(plan, reductions[b], cell_t.data() + 9 * b, request.cutoff);
+            const CellPlan outcome = outcomes[b];
             const int64_t bins = outcome == CellPlan::kReady
                 ? int64_t{plan.dims[0]} * plan.dims[1] * plan.dims[2] : 0;
             if (outcome != CellPlan::kReady || total_bins + bins > kMaximumTotalBins) {

@@ -6,13 +6,13 @@
 // and the image ranges must come out bit-identical to the reference's.
 // Structures are independent, so large batches are split over host threads.
 #include "tnr_geometry.h"
+#include "tnr_pool.h"
 
 #include <algorithm>
 #include <cmath>
 #include <string>
 #include <limits>
 #include <mutex>
-#include <thread>
 
 namespace tnr {
 namespace {
@@ -161,20 +161,7 @@ PeriodicGeometry build_geometry(const double* cells, const uint8_t* pbc,
             }
         }
     };
-    const unsigned hardware = std::max(1u, std::thread::hardware_concurrency());
-    const int64_t workers = std::min<int64_t>(hardware, batch / 512);
-    if (workers <= 1) {
-        run(0, batch);
-    } else {
-        std::vector<std::thread> threads;
-        const int64_t chunk = (batch + workers - 1) / workers;
-        for (int64_t w = 0; w < workers; ++w) {
-            const int64_t begin = w * chunk;
-            const int64_t end = std::min(batch, begin + chunk);
-            threads.emplace_back(run, begin, end);
-        }
-        for (auto& thread : threads) thread.join();
-    }
+    HostPool::instance().parallel_for(batch, 128, run);
     geometry.image_begin.assign(static_cast<size_t>(batch + 1), 0);
     for (int64_t b = 0; b < batch; ++b) {
         if (b == failed_at) throw InputError(failure);

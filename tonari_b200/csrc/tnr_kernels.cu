@@ -274,13 +274,17 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
             record.x = g[0];
             record.y = g[1];
             record.z = g[2];
-            record.w = index_to_lane(static_cast<int32_t>(atom), T(0));
+            // Order key of the image (2a + 1 for the zero image, 2a + 2
+            // otherwise; read by the search kernels).
+            record.w = index_to_lane(static_cast<int32_t>(2u * static_cast<uint32_t>(atom) +
+                                                          (k == center ? 1u : 2u)),
+                                     T(0));
             reinterpret_cast<V*>(args.ghost_pos)[slot] = record;
             V original;
             original.x = args.positions[3 * atom];
             original.y = args.positions[3 * atom + 1];
             original.z = args.positions[3 * atom + 2];
-            original.w = record.w;
+            original.w = index_to_lane(static_cast<int32_t>(atom), T(0));
             reinterpret_cast<V*>(args.ghost_orig)[slot] = original;
             const int4 image = args.image_shift[plan.image_begin + k];
             args.ghost_meta[slot] = make_int4(image.x - wrap[0], image.y - wrap[1],
@@ -357,10 +361,13 @@ struct StencilRows {
 template <typename T>
 __device__ __forceinline__ void bin_coordinates(const StructurePlan<T>& plan, int64_t bin,
                                                 int32_t& bx, int32_t& by, int32_t& bz) {
-    const int64_t local = bin - plan.bin_begin;
-    bz = static_cast<int32_t>(local % plan.dims[2]);
-    by = static_cast<int32_t>((local / plan.dims[2]) % plan.dims[1]);
-    bx = static_cast<int32_t>(local / (static_cast<int64_t>(plan.dims[2]) * plan.dims[1]));
+    // A structure has fewer than 2^26 bins: 32-bit division suffices.
+    const uint32_t local = static_cast<uint32_t>(bin - plan.bin_begin);
+    const uint32_t column = local / static_cast<uint32_t>(plan.dims[2]);
+    bz = static_cast<int32_t>(local - column * static_cast<uint32_t>(plan.dims[2]));
+    const uint32_t plane = column / static_cast<uint32_t>(plan.dims[1]);
+    by = static_cast<int32_t>(column - plane * static_cast<uint32_t>(plan.dims[1]));
+    bx = static_cast<int32_t>(plane);
 }
 
 // Lanes 0-8 fetch the slot range of one stencil row each and the warp builds
@@ -459,78 +466,90 @@ __global__ void __launch_bounds__(kBinThreads) stencil_words_kernel(SearchArgs<T
     }
 }
 
-// Count pass, lanes = sources: the warp serves up to 32 source atoms of its
-// bin at once.  Per 32-candidate chunk every lane loads one candidate record
-// into shared memory; each record is then read back as a broadcast and
-// tested against all lanes' sources, so one short instruction sequence
-// evaluates 32 source-candidate pairs.  Candidates in the band shell, the
-// zero-shift self pair and (half list) periodic self images are flagged in a
-// per-lane bit word and decided after the chunk.  Accepted-candidate bits are
-// stored transposed -- word w of source rank r at base + w * S + r, S the
-// bin's source count -- so each chunk's store is coalesced.
-// Spreads the low 32/G bits of x to positions 0, G, 2G, ... (G a power of
-// two), by successive doubling of the gaps.
-template <int G>
-__device__ __forceinline__ uint32_t spread_bits(uint32_t x) {
-    if constexpr (G == 1) {
-        return x;
-    } else {
-        // Each step doubles the distance between the remaining bit groups.
-        uint32_t y = x;
-        if constexpr (G >= 2) {
-            y = (y | (y << 8)) & 0x00ff00ffu;
-            y = (y | (y << 4)) & 0x0f0f0f0fu;
-            y = (y | (y << 2)) & 0x33333333u;
-            y = (y | (y << 1)) & 0x55555555u;  // 16 bits -> even positions
-        }
-        if constexpr (G >= 4) {
-            // 8 bits now sit at even positions 0..14; spread them to 0, 4, ..., 28.
-            uint32_t z = 0;
-#pragma unroll
-            for (int b = 0; b < 32 / G; ++b) z |= ((y >> (2 * b)) & 1u) << (G * b);
-            y = z;
-        }
-        return y;
-    }
+// Packed pairs of floats (sm_100 f32x2 arithmetic): two source-candidate
+// screening tests per instruction in the count pass.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// Squared distances of one point (packed as (c, c) per axis) to two sources;
+// per element exactly screen_distance2 below.
+__device__ __forceinline__ unsigned long long distance2_pair(
+    unsigned long long cx, unsigned long long cy, unsigned long long cz,
+    unsigned long long sx, unsigned long long sy, unsigned long long sz) {
+    unsigned long long dx, dy, dz, d2;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(dx) : "l"(cx), "l"(sx));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(dy) : "l"(cy), "l"(sy));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(dz) : "l"(cz), "l"(sz));
+    asm("mul.rn.f32x2 %0, %1, %1;" : "=l"(d2) : "l"(dx));
+    asm("fma.rn.f32x2 %0, %1, %1, %0;" : "+l"(d2) : "l"(dy));
+    asm("fma.rn.f32x2 %0, %1, %1, %0;" : "+l"(d2) : "l"(dz));
+    return d2;
 }
 
-// Tests one 32-candidate tile against this lane's source.  With G lane groups
-// the lane takes candidates j = my_group + G * jj; the bits are accumulated
-// compactly (bit jj) with compile-time shifts and spread once at the end.
-template <typename T, bool Half, int G>
-__device__ __forceinline__ void test_tile(const vec4_t<T>* tile, const vec4_t<T>& qs,
-                                          int32_t source, T inner2, T search2, int my_group,
-                                          uint32_t& bits, uint32_t& search_bits) {
-    uint32_t inner_compact = 0, search_compact = 0;
-#pragma unroll
-    for (int jj = 0; jj < 32 / G; ++jj) {
-        const vec4_t<T> g = tile[my_group + G * jj];
-        const T dx = g.x - qs.x;
-        const T dy = g.y - qs.y;
-        const T dz = g.z - qs.z;
-        const T d2 = dx * dx + dy * dy + dz * dz;
-        bool in_inner = d2 < inner2;
-        bool in_search = d2 < search2;
-        if constexpr (Half) {
-            const int32_t order = lane_to_index(g.w) - source;
-            in_inner = in_inner && order > 0;
-            in_search = in_search && order >= 0;
-        }
-        inner_compact |= static_cast<uint32_t>(in_inner) << jj;
-        search_compact |= static_cast<uint32_t>(in_search) << jj;
-    }
-    bits = spread_bits<G>(inner_compact) << my_group;
-    search_bits = spread_bits<G>(search_compact) << my_group;
+// The screening distance in scalar form, with explicit roundings so that the
+// rare path re-derives exactly the main test's decisions.
+__device__ __forceinline__ float screen_distance2(float cx, float cy, float cz, float sx, float sy,
+                                                  float sz) {
+    const float dx = __fsub_rn(cx, sx), dy = __fsub_rn(cy, sy), dz = __fsub_rn(cz, sz);
+    return __fmaf_rn(dz, dz, __fmaf_rn(dy, dy, __fmul_rn(dx, dx)));
+}
+__device__ __forceinline__ double screen_distance2(double cx, double cy, double cz, double sx,
+                                                   double sy, double sz) {
+    const double dx = __dsub_rn(cx, sx), dy = __dsub_rn(cy, sy), dz = __dsub_rn(cz, sz);
+    return __fma_rn(dz, dz, __fma_rn(dy, dy, __dmul_rn(dx, dx)));
 }
 
+// 32 x 32 bit-matrix transpose across a warp: on entry bit r of lane c's x
+// is element (c, r); on return bit c of lane r's value is that element.
+// Five butterfly stages exchange the off-diagonal blocks of width j.
+__device__ __forceinline__ uint32_t transpose_bits32(uint32_t x, int lane) {
+    const uint32_t low_masks[5] = {0x0000ffffu, 0x00ff00ffu, 0x0f0f0f0fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+    for (int stage = 0; stage < 5; ++stage) {
+        const int j = 16 >> stage;
+        const uint32_t m = low_masks[stage];
+        const uint32_t y = __shfl_xor_sync(kFullMask, x, j);
+        x = (lane & j) ? ((x & ~m) | ((y & ~m) >> j)) : ((x & m) | ((y & m) << j));
+    }
+    return x;
+}
+
+// Count pass, lanes = candidates: the warp serves one bin.  Each lane holds
+// one candidate of the bin's stencil (32 per tile) in registers; the bin's
+// sources are staged once in shared memory (up to 32 at a time, structure of
+// arrays) and read back as broadcasts, four per vector load.  Each lane tests
+// its candidate against every source -- for float two sources per packed
+// f32x2 instruction -- and collects one bit per source; a 32 x 32 bit
+// transpose across the warp then gives every source its mask word for the
+// tile.  The lanes stay busy whatever the bin's source count.
+//
+// Half lists compare order keys instead of atom indices.  The ghost record's
+// fourth lane carries key 2a + 1 for the zero image of atom a and 2a + 2 for
+// its other images (written by the scatter); a source's key is 2a + 1.
+// Key(c) > key(s) + 1 means atom(c) > atom(s) (accepted by distance alone);
+// key(c) == key(s) + 1 is a periodic image of the source itself (decided by
+// its shift in the rare path); key(c) == key(s) is the zero-shift self pair,
+// which the test neither accepts nor flags and which is set afterwards per
+// include_self.  Full lists accept the self pair by distance (d = 0) and fix
+// it the same way.  Candidates in the band shell are flagged per lane and the
+// flagged lanes re-run their sources to decide them exactly.
+// Accepted-candidate bits are stored transposed -- word w of source rank r at
+// base + w * S + r, S the bin's source count -- one coalesced store per tile.
 template <typename T, bool Half>
 __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
     __shared__ StencilRows stencil[kSearchWarps];
-    __shared__ V tile[kSearchWarps][32];
-    __shared__ int32_t tile_slot[kSearchWarps][32];
-    __shared__ int4 tile_meta[kSearchWarps][32];
-    __shared__ V tile_orig[kSearchWarps][32];
+    // Sources of the current block, structure of arrays (16-byte aligned
+    // rows so four consecutive sources load as one vector).
+    __shared__ __align__(16) T source_x[kSearchWarps][32];
+    __shared__ __align__(16) T source_y[kSearchWarps][32];
+    __shared__ __align__(16) T source_z[kSearchWarps][32];
+    __shared__ __align__(16) uint32_t source_key[kSearchWarps][32];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -548,45 +567,24 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
         uint32_t* mask = args.mask_words + args.bin_word_start[bin];
         const T search2 = plan.search_squared;
         const T inner2 = plan.inner_squared;
-        V* my_tile = tile[warp];
-        int32_t* my_slot = tile_slot[warp];
 
-        // Lane groups: with S <= 16 sources the warp splits into G = 32 / P groups
-        // of P lanes (P = next power of two >= S); group g tests candidates
-        // j = g, g + G, ... of each chunk against its P sources, and the groups'
-        // bits are OR-combined afterwards.
-        const uint32_t width = n_sources >= 32 ? 32u : (n_sources <= 1 ? 1u : 1u << (32 - __clz(n_sources - 1)));
-        const int groups = 32 / static_cast<int>(width);
-        const int my_group = lane / static_cast<int>(width);
-        const uint32_t my_rank = static_cast<uint32_t>(lane) % width;
-
-        for (uint32_t base = 0; base < n_sources; base += width) {
-            const uint32_t rank = base + my_rank;
-            const bool active = rank < n_sources;
-            int32_t source = -1;
-            // Idle lanes test against a NaN position: no candidate is ever inner
-            // or rare for them, so they never reach the exact test.
-            V qs;
-            qs.x = qs.y = qs.z = qs.w = static_cast<T>(NAN);
-            int32_t self = -1;
-            long long ws[3] = {0, 0, 0};
-            T ps[3] = {T(0), T(0), T(0)};
-            if (active) {
-                source = args.source_list[first_source + rank];
-                qs = reinterpret_cast<const V*>(args.wrapped)[source];
-                self = args.self_slot[source];
-                ws[0] = args.wraps[3 * source];
-                ws[1] = args.wraps[3 * source + 1];
-                ws[2] = args.wraps[3 * source + 2];
-                ps[0] = args.positions[3 * source];
-                ps[1] = args.positions[3 * source + 1];
-                ps[2] = args.positions[3 * source + 2];
-            }
-            // Candidate index of the source's own zero image: its bit is set
-            // or cleared per include_self after each chunk instead of going
-            // through the exact test.
-            int32_t self_k = -1;
-            if (active) {
+        for (uint32_t base = 0; base < n_sources; base += 32) {
+            const int block = static_cast<int>(min(32u, n_sources - base));
+            // Sources are padded to a multiple of four with NaN positions,
+            // which no candidate is ever accepted for or in the band of.
+            const int padded = (block + 3) & ~3;
+            int32_t my_source = -1;
+            int32_t self_k = -1;  // candidate index of my source's zero image
+            __syncwarp();
+            if (lane < block) {
+                my_source = args.source_list[first_source + base + lane];
+                const V q = reinterpret_cast<const V*>(args.wrapped)[my_source];
+                source_x[warp][lane] = q.x;
+                source_y[warp][lane] = q.y;
+                source_z[warp][lane] = q.z;
+                source_key[warp][lane] = Half ? 2u * static_cast<uint32_t>(my_source) + 1u
+                                              : static_cast<uint32_t>(my_source);
+                const int32_t self = args.self_slot[my_source];
 #pragma unroll
                 for (int r = 0; r < 9; ++r) {
                     const int32_t begin_r = rows.prefix[r] + rows.delta[r];
@@ -595,95 +593,136 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                         self_k = rows.prefix[r] + (self - begin_r);
                     }
                 }
+            } else if (lane < padded) {
+                source_x[warp][lane] = source_y[warp][lane] = source_z[warp][lane] =
+                    static_cast<T>(NAN);
+                source_key[warp][lane] = 0u;
             }
-            const bool self_mine = self_k >= 0 && ((self_k & 31) % groups) == my_group;
+            __syncwarp();
             uint32_t count = 0;
-            // Per-lane cursor over the concatenated stencil rows: candidate k
-            // = 32 w + lane lives in row `row` at slot k + delta[row]; the row
-            // advances by at most a few steps per chunk.  The next chunk's
-            // record is loaded while the current tile is tested.
+            // This lane's candidate of tile w, loaded one tile ahead.  The
+            // lane walks the stencil rows forward (k grows by 32 per tile):
+            // `row` is the row holding k, row_end its end.
             int32_t row = 0;
-            auto record_of = [&](int32_t k, int32_t& slot_out) {
-                V rec;
+            int32_t row_end = rows.prefix[1];
+            auto load_candidate = [&](int32_t w, V& record, int32_t& slot) {
+                const int32_t k = 32 * w + lane;
                 if (k < total) {
-                    while (rows.prefix[row + 1] <= k) ++row;
-                    slot_out = k + rows.delta[row];
-                    rec = reinterpret_cast<const V*>(args.ghost_pos)[slot_out];
+                    while (k >= row_end) row_end = rows.prefix[++row + 1];
+                    slot = k + rows.delta[row];
+                    record = reinterpret_cast<const V*>(args.ghost_pos)[slot];
                 } else {
-                    slot_out = -1;
-                    rec.x = static_cast<T>(INFINITY);
-                    rec.y = T(0);
-                    rec.z = T(0);
-                    rec.w = index_to_lane(-1, T(0));
+                    slot = -1;
+                    record.x = static_cast<T>(INFINITY);
+                    record.y = T(0);
+                    record.z = T(0);
+                    record.w = index_to_lane(0, T(0));
                 }
-                return rec;
             };
-            int32_t next_slot = -1;
-            V next_record = record_of(lane, next_slot);
+            V next;
+            int32_t next_slot;
+            load_candidate(0, next, next_slot);
+            uint32_t* mask_out = mask + base + lane;  // word w of my source at w * n_sources
             for (int32_t w = 0; w < words; ++w) {
-                const V record = next_record;
-                const int32_t record_slot = next_slot;
-                if (w + 1 < words) next_record = record_of(32 * (w + 1) + lane, next_slot);
-                __syncwarp();
-                my_tile[lane] = record;
-                my_slot[lane] = record_slot;
-                __syncwarp();
-                uint32_t bits = 0;
-                uint32_t search_bits = 0;
-                switch (groups) {
-                    case 1: test_tile<T, Half, 1>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
-                    case 2: test_tile<T, Half, 2>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
-                    case 4: test_tile<T, Half, 4>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
-                    case 8: test_tile<T, Half, 8>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
-                    case 16: test_tile<T, Half, 16>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
-                    default: test_tile<T, Half, 32>(my_tile, qs, source, inner2, search2, my_group, bits, search_bits); break;
+                const V cand = next;
+                const int32_t slot = next_slot;
+                if (w + 1 < words) load_candidate(w + 1, next, next_slot);
+                const uint32_t cand_key = static_cast<uint32_t>(lane_to_index(cand.w));
+                uint32_t key = 0, key_less = 0;  // key(c) and key(c) - 1
+                unsigned long long cx = 0, cy = 0, cz = 0;
+                if constexpr (std::is_same<T, float>::value) {
+                    cx = pack2(cand.x, cand.x);
+                    cy = pack2(cand.y, cand.y);
+                    cz = pack2(cand.z, cand.z);
                 }
-                uint32_t rare_bits = search_bits & ~bits;
-                if (self_mine && (self_k >> 5) == w) {
-                    const uint32_t bit = 1u << (self_k & 31);
-                    bits = args.include_self ? (bits | bit) : (bits & ~bit);
-                    rare_bits &= ~bit;
+                if constexpr (Half) {
+                    key = cand_key;  // 0 for an empty lane
+                    key_less = key - 1u;
                 }
-                if (!active) rare_bits = 0;
-                if (__any_sync(kFullMask, rare_bits != 0u)) {
-                    // Rare candidates in this chunk: stage the chunk's ghost
-                    // shifts and original target positions once, then decide
-                    // each rare candidate from shared memory.
-                    if (record_slot >= 0) {
-                        tile_meta[warp][lane] = args.ghost_meta[record_slot];
-                        tile_orig[warp][lane] = reinterpret_cast<const V*>(args.ghost_orig)[record_slot];
+                // Bit r of keep_bits: this lane's candidate is accepted for
+                // source r.  rare: some source has it in its band.
+                uint32_t keep_bits = 0;
+                bool rare = false;
+                for (int r0 = 0; r0 < padded; r0 += 4) {
+                    T d2[4];
+                    if constexpr (std::is_same<T, float>::value) {
+                        const ulonglong2 sx = *reinterpret_cast<const ulonglong2*>(&source_x[warp][r0]);
+                        const ulonglong2 sy = *reinterpret_cast<const ulonglong2*>(&source_y[warp][r0]);
+                        const ulonglong2 sz = *reinterpret_cast<const ulonglong2*>(&source_z[warp][r0]);
+                        unpack2(distance2_pair(cx, cy, cz, sx.x, sy.x, sz.x), d2[0], d2[1]);
+                        unpack2(distance2_pair(cx, cy, cz, sx.y, sy.y, sz.y), d2[2], d2[3]);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            d2[u] = screen_distance2(cand.x, cand.y, cand.z, source_x[warp][r0 + u],
+                                                     source_y[warp][r0 + u], source_z[warp][r0 + u]);
+                        }
                     }
-                    __syncwarp();
-                    while (rare_bits) {
-                        const int j = __ffs(rare_bits) - 1;
-                        rare_bits &= rare_bits - 1;
-                        const V g = my_tile[j];
-                        const int4 meta = tile_meta[warp][j];
-                        const long long shift[3] = {meta.x + ws[0], meta.y + ws[1], meta.z + ws[2]};
-                        bool keep = true;
+                    const uint4 keys = *reinterpret_cast<const uint4*>(&source_key[warp][r0]);
+                    const uint32_t key_of[4] = {keys.x, keys.y, keys.z, keys.w};
+                    uint32_t nibble = 0;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        bool keep = d2[u] < inner2;
+                        bool band = d2[u] < search2;
+                        if constexpr (Half) {
+                            keep = keep && key_less > key_of[u];
+                            band = band && key > key_of[u];
+                        }
+                        if (keep) nibble |= 1u << u;
+                        rare = rare | (band & !keep);
+                    }
+                    keep_bits |= nibble << r0;
+                }
+                if (__any_sync(kFullMask, rare) && rare) {
+                    // Rare: band shell, or a half-list periodic image of the
+                    // source itself; decided exactly by the candidate's lane.
+                    for (int r = 0; r < block; ++r) {
+                        const T d2 = screen_distance2(cand.x, cand.y, cand.z, source_x[warp][r],
+                                                      source_y[warp][r], source_z[warp][r]);
+                        const uint32_t key_r = source_key[warp][r];
+                        bool keep = d2 < inner2;
+                        bool band = d2 < search2;
+                        if constexpr (Half) {
+                            keep = keep && key_less > key_r;
+                            band = band && key > key_r;
+                        }
+                        if (!band || keep) continue;
+                        const int32_t source = static_cast<int32_t>(Half ? key_r >> 1 : key_r);
+                        const int4 meta = args.ghost_meta[slot];  // .w: the candidate's atom
+                        const long long shift[3] = {
+                            meta.x + static_cast<long long>(args.wraps[3 * source]),
+                            meta.y + static_cast<long long>(args.wraps[3 * source + 1]),
+                            meta.z + static_cast<long long>(args.wraps[3 * source + 2])};
+                        keep = true;
                         if (Half && meta.w == source) keep = canonical_shift(shift);
-                        const T dx = g.x - qs.x;
-                        const T dy = g.y - qs.y;
-                        const T dz = g.z - qs.z;
-                        if (keep && !((dx * dx + dy * dy + dz * dz) < inner2)) {
-                            const V pt = tile_orig[warp][j];
-                            const T vx = exact_component(pt.x, ps[0], shift, plan.cell, 0);
-                            const T vy = exact_component(pt.y, ps[1], shift, plan.cell, 1);
-                            const T vz = exact_component(pt.z, ps[2], shift, plan.cell, 2);
+                        if (keep && !(d2 < inner2)) {
+                            const V pt = reinterpret_cast<const V*>(args.ghost_orig)[slot];
+                            const T vx = exact_component(pt.x, args.positions[3 * source], shift, plan.cell, 0);
+                            const T vy = exact_component(pt.y, args.positions[3 * source + 1], shift, plan.cell, 1);
+                            const T vz = exact_component(pt.z, args.positions[3 * source + 2], shift, plan.cell, 2);
                             keep = exact_norm2(vx, vy, vz) < plan.cutoff_squared;
                         }
-                        if (keep) bits |= 1u << j;
+                        if (keep) keep_bits |= 1u << r;
                     }
                 }
-                for (int offset = static_cast<int>(width); offset < 32; offset <<= 1) {
-                    bits |= __shfl_xor_sync(kFullMask, bits, offset);
+                // Transpose the warp's 32 x 32 bit matrix: afterwards lane r
+                // holds source r's word (bit c = candidate lane c accepted).
+                const uint32_t my_word_bits = transpose_bits32(keep_bits, lane);
+                if (lane < block) {
+                    uint32_t my_word = my_word_bits;
+                    if ((self_k >> 5) == w) {
+                        const uint32_t bit = 1u << (self_k & 31);
+                        my_word = args.include_self ? (my_word | bit) : (my_word & ~bit);
+                    }
+                    *mask_out = my_word;
+                    count += __popc(my_word);
                 }
-                if (!active) bits = 0;
-                if (active && my_group == 0) mask[static_cast<int64_t>(w) * n_sources + rank] = bits;
-                count += __popc(bits);
+                mask_out += n_sources;
             }
-            if (active && my_group == 0) {
-                args.counts[args.source_order ? static_cast<int64_t>(first_source + rank) : source] = count;
+            if (lane < block) {
+                args.counts[args.source_order ? static_cast<int64_t>(first_source + base + lane)
+                                              : my_source] = count;
                 if (count > static_cast<uint32_t>(INT_MAX)) {
                     atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
                 }
@@ -770,7 +809,9 @@ __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const Str
                                        mul_rn(s1, cell[5])), mul_rn(s2, cell[8]));
             }
         } else {
-            target = lane_to_index(reinterpret_cast<const V*>(args.ghost_pos)[slot].w);
+            const uint32_t key =
+                static_cast<uint32_t>(lane_to_index(reinterpret_cast<const V*>(args.ghost_pos)[slot].w));
+            target = static_cast<int32_t>((key - 1u) >> 1);
         }
         const int64_t s = source + args.index_offset;
         const int64_t t = target + args.index_offset;
