@@ -948,56 +948,71 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
 
 // Write pass for unsorted calls.  In cell order any 32 consecutive sources
 // own one contiguous output range, whatever bins they belong to, so one warp
-// takes 32 consecutive sources, one per lane, each with its own stencil-row
-// table.  In every round each lane that still has pairs takes its next
-// accepted candidate from its bitmask words and emits one pair; the round's
-// rows are assigned by a ballot prefix, so each store instruction covers one
-// contiguous run of rows.
+// takes 32 consecutive sources and may write their pairs in any order inside
+// that range.  The sources' stencil-row tables, positions, wraps and cells
+// are staged in shared memory.  Work is handed out per bitmask word: the warp
+// loads word w of all 32 sources at once (one coalesced load; the next batch
+// is already in flight), and a lane whose word is used up takes the next
+// nonzero word of the batch, so every lane stays busy however unequal the
+// sources' pair counts are (half lists make them very unequal).  In each
+// round every busy lane takes one accepted candidate of its word, the ghost
+// records of that pair are loaded a round ahead, and the round's rows are
+// assigned by a ballot prefix so that each store covers one contiguous run.
+constexpr int kEmitPerLane = 4;
+constexpr int kEmitQueue = 32 * kEmitPerLane;
+
+template <typename T>
+struct EmitShared {
+    StencilRows rows[32];
+    vec4_t<T> pos[32];  // original source position
+    int4 wrap[32];      // source wraps; .w = source atom
+    __align__(32) T cell[32][12];  // source's cell rows, padded for vector loads
+    int2 mailbox[32];
+    int2 queue[2][kEmitQueue];  // (ghost slot, source lane), double buffered
+};
+
+constexpr int kEmitThreads = 128;
+
 template <typename T, int Q>
-__global__ void __launch_bounds__(kSearchThreads) cell_emit_kernel(SearchArgs<T> args) {
+__global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
-    __shared__ StencilRows lane_rows[kSearchWarps][32];
+    __shared__ EmitShared<T> shared[kEmitThreads / 32];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const unsigned below = (1u << lane) - 1u;
     const bool need_vector = wants<Q>(args.out_d, kQ_d) || wants<Q>(args.out_D, kQ_D);
     const bool need_shift = wants<Q>(args.out_S, kQ_S) || need_vector;
+    EmitShared<T>& sh = shared[warp];
     const int64_t n_groups = (args.n_sources + 31) / 32;
     const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
     for (int64_t group = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
          group < n_groups; group += stride) {
         const int64_t k = group * 32 + lane;
         const bool valid = k < args.n_sources;
-        int32_t remaining = 0;
-        int32_t source = 0, words = 0, word_index = -1;
-        uint32_t word = 0;
+        int32_t words = 0;
         const uint32_t* mask = nullptr;
         int64_t mask_stride = 0;
-        const StructurePlan<T>* plan = nullptr;
-        T ps[3] = {T(0), T(0), T(0)};
-        int32_t ws[3] = {0, 0, 0};
-        StencilRows& rows = lane_rows[warp][lane];
+        __syncwarp();  // the previous group's shared data is no longer read
         if (valid) {
-            source = args.source_list[k];
-            remaining = static_cast<int32_t>(args.counts[k]);
+            const int32_t source = args.source_list[k];
             const int32_t bin = args.source_bin[k];
             const uint32_t first = static_cast<uint32_t>(args.bin_start[bin] >> 32);
             const uint32_t n_bin_sources = static_cast<uint32_t>(args.bin_start[bin + 1] >> 32) - first;
-            plan = &args.plans[args.bin_struct[bin]];
+            const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
             int32_t bx, by, bz;
-            bin_coordinates(*plan, bin, bx, by, bz);
-            // This lane's stencil rows and prefix table.
+            bin_coordinates(plan, bin, bx, by, bz);
+            StencilRows& rows = sh.rows[lane];
             int32_t prefix = 0;
 #pragma unroll
             for (int r = 0; r < 9; ++r) {
                 int32_t begin = 0, length = 0;
                 const int32_t x = bx + r / 3 - 1;
                 const int32_t y = by + r % 3 - 1;
-                if (x >= 0 && x < plan->dims[0] && y >= 0 && y < plan->dims[1]) {
+                if (x >= 0 && x < plan.dims[0] && y >= 0 && y < plan.dims[1]) {
                     const int32_t z0 = max(bz - 1, 0);
-                    const int32_t z1 = min(bz + 1, plan->dims[2] - 1);
-                    const int64_t row = plan->bin_begin +
-                        (static_cast<int64_t>(x) * plan->dims[1] + y) * plan->dims[2];
+                    const int32_t z1 = min(bz + 1, plan.dims[2] - 1);
+                    const int64_t row = plan.bin_begin +
+                        (static_cast<int64_t>(x) * plan.dims[1] + y) * plan.dims[2];
                     begin = static_cast<int32_t>(args.bin_start[row + z0] & 0xffffffffull);
                     length = static_cast<int32_t>(args.bin_start[row + z1 + 1] & 0xffffffffull) - begin;
                 }
@@ -1011,70 +1026,136 @@ __global__ void __launch_bounds__(kSearchThreads) cell_emit_kernel(SearchArgs<T>
             words = (prefix + 31) >> 5;
             mask = args.mask_words + args.bin_word_start[bin] + (k - first);
             mask_stride = n_bin_sources;
-            ps[0] = args.positions[3 * source];
-            ps[1] = args.positions[3 * source + 1];
-            ps[2] = args.positions[3 * source + 2];
-            ws[0] = args.wraps[3 * source];
-            ws[1] = args.wraps[3 * source + 1];
-            ws[2] = args.wraps[3 * source + 2];
-        }
-        int64_t out_row = args.pair_start[min(group * 32, args.n_sources - 1)];
-        // Next accepted candidate of this lane (bitmask walk).
-        auto next_slot = [&]() -> int32_t {
-            while (word == 0u && word_index + 1 < words) {
-                ++word_index;
-                word = mask[static_cast<int64_t>(word_index) * mask_stride];
+            V ps;
+            ps.x = args.positions[3 * source];
+            ps.y = args.positions[3 * source + 1];
+            ps.z = args.positions[3 * source + 2];
+            ps.w = T(0);
+            sh.pos[lane] = ps;
+            sh.wrap[lane] = make_int4(args.wraps[3 * source], args.wraps[3 * source + 1],
+                                      args.wraps[3 * source + 2], source);
+            if (need_vector) {
+#pragma unroll
+                for (int c = 0; c < 9; ++c) sh.cell[lane][c] = plan.cell[c];
             }
-            const int32_t bit = __ffs(word) - 1;
-            word &= word - 1u;
-            return slot_of(rows, 32 * word_index + bit);
+        }
+        const int32_t batches = static_cast<int32_t>(__reduce_max_sync(kFullMask, static_cast<unsigned>(words)));
+        __syncwarp();
+        int64_t out_row = args.pair_start[group * 32];
+
+        // Word batches: lane l holds word `batch` of source l; the next batch
+        // is loaded one batch ahead.  `avail`: nonzero words not yet taken.
+        int32_t batch = 0;
+        uint32_t stage = words > 0 ? mask[0] : 0u;
+        uint32_t stage_next = words > 1 ? mask[mask_stride] : 0u;
+        unsigned avail = __ballot_sync(kFullMask, stage != 0u);
+        uint32_t bits = 0;  // this lane's current word (untaken candidates)
+        int32_t my_r = 0, my_w = 0;
+        auto refill = [&]() {
+            while (true) {
+                const unsigned need = __ballot_sync(kFullMask, bits == 0u);
+                if (need == 0u) return;
+                if (avail == 0u) {
+                    if (batch + 1 >= batches) return;
+                    ++batch;
+                    stage = stage_next;
+                    stage_next = batch + 1 < words ? mask[(batch + 1) * mask_stride] : 0u;
+                    avail = __ballot_sync(kFullMask, stage != 0u);
+                    continue;
+                }
+                // Hand the batch's untaken nonzero words to the lanes in
+                // need, in rank order, through a shared mailbox.
+                const int32_t n_avail = __popc(avail);
+                const bool offering = (avail >> lane) & 1u;
+                const int32_t offer_rank = __popc(avail & below);
+                if (offering) sh.mailbox[offer_rank] = make_int2(static_cast<int32_t>(stage), lane);
+                __syncwarp();
+                const int32_t rank = __popc(need & below);
+                if (bits == 0u && rank < n_avail) {
+                    const int2 handed = sh.mailbox[rank];
+                    bits = static_cast<uint32_t>(handed.x);
+                    my_r = handed.y;
+                    my_w = batch;
+                }
+                avail = __ballot_sync(kFullMask, offering && offer_rank >= __popc(need));
+                __syncwarp();
+            }
         };
-        // Software pipeline: the records of round r+1 are in flight while
-        // round r is computed and stored.
-        int4 meta = make_int4(0, 0, 0, 0);
-        V pt{};
-        if (remaining > 0) {
-            const int32_t slot = next_slot();
-            meta = args.ghost_meta[slot];
-            if (need_vector) pt = reinterpret_cast<const V*>(args.ghost_orig)[slot];
-        }
-        while (__any_sync(kFullMask, remaining > 0)) {
-            const bool active = remaining > 0;
-            const int4 cur_meta = meta;
-            const V cur_pt = pt;
-            if (remaining > 1) {
-                const int32_t slot = next_slot();
-                meta = args.ghost_meta[slot];
-                if (need_vector) pt = reinterpret_cast<const V*>(args.ghost_orig)[slot];
+        // Selection rounds fill a queue of (slot, source) entries and need no
+        // global loads but the staged mask words.  The queue is double
+        // buffered: the ghost records of chunk c (up to kEmitPerLane per
+        // lane) are requested, the next chunk is selected while they are in
+        // flight, and only then is chunk c computed and stored.
+        auto fill = [&](int2* queue) -> int32_t {
+            int32_t queued = 0;
+            while (queued <= kEmitQueue - 32) {
+                refill();
+                const bool has = bits != 0u;
+                const unsigned ballot = __ballot_sync(kFullMask, has);
+                if (ballot == 0u) break;
+                if (has) {
+                    const int32_t bit = __ffs(bits) - 1;
+                    bits &= bits - 1u;
+                    queue[queued + __popc(ballot & below)] =
+                        make_int2(slot_of(sh.rows[my_r], 32 * my_w + bit), my_r);
+                }
+                queued += __popc(ballot);
             }
-            --remaining;
-            const unsigned ballot = __ballot_sync(kFullMask, active);
-            const int64_t o = out_row + __popc(ballot & below);
-            out_row += __popc(ballot);
-            if (active) {
-                const int64_t target = cur_meta.w;
+            __syncwarp();
+            return queued;
+        };
+        int32_t current = 0;
+        int32_t queued = fill(sh.queue[0]);
+        while (queued > 0) {
+            const int2* queue = sh.queue[current];
+            int4 meta[kEmitPerLane];
+            V pt[kEmitPerLane];
+            int32_t source_r[kEmitPerLane];
+#pragma unroll
+            for (int m = 0; m < kEmitPerLane; ++m) {
+                const int32_t e = lane + 32 * m;
+                source_r[m] = 0;
+                if (e < queued) {
+                    const int2 entry = queue[e];
+                    source_r[m] = entry.y;
+                    meta[m] = args.ghost_meta[entry.x];
+                    if (need_vector) pt[m] = reinterpret_cast<const V*>(args.ghost_orig)[entry.x];
+                }
+            }
+            const int32_t next_queued = fill(sh.queue[current ^ 1]);
+#pragma unroll
+            for (int m = 0; m < kEmitPerLane; ++m) {
+                const int32_t e = lane + 32 * m;
+                if (e < queued) {
+                const int64_t o = out_row + e;
+                const int32_t r = source_r[m];
+                const int4 ws = sh.wrap[r];
                 int32_t shift[3] = {0, 0, 0};
                 T vec[3] = {T(0), T(0), T(0)};
                 if (need_shift) {
                     // Cell-list shifts fit int32 by construction of the plan.
-                    shift[0] = cur_meta.x + ws[0];
-                    shift[1] = cur_meta.y + ws[1];
-                    shift[2] = cur_meta.z + ws[2];
+                    shift[0] = meta[m].x + ws.x;
+                    shift[1] = meta[m].y + ws.y;
+                    shift[2] = meta[m].z + ws.z;
                 }
                 if (need_vector) {
+                    const V ps = sh.pos[r];
+                    const V c0 = reinterpret_cast<const V*>(sh.cell[r])[0];
+                    const V c1 = reinterpret_cast<const V*>(sh.cell[r])[1];
+                    const V c2 = reinterpret_cast<const V*>(sh.cell[r])[2];
+                    const T cell[9] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w, c2.x};
                     const T s0 = static_cast<T>(shift[0]);
                     const T s1 = static_cast<T>(shift[1]);
                     const T s2 = static_cast<T>(shift[2]);
-                    const T* cell = plan->cell;
-                    vec[0] = add_rn(add_rn(add_rn(sub_rn(cur_pt.x, ps[0]), mul_rn(s0, cell[0])),
+                    vec[0] = add_rn(add_rn(add_rn(sub_rn(pt[m].x, ps.x), mul_rn(s0, cell[0])),
                                            mul_rn(s1, cell[3])), mul_rn(s2, cell[6]));
-                    vec[1] = add_rn(add_rn(add_rn(sub_rn(cur_pt.y, ps[1]), mul_rn(s0, cell[1])),
+                    vec[1] = add_rn(add_rn(add_rn(sub_rn(pt[m].y, ps.y), mul_rn(s0, cell[1])),
                                            mul_rn(s1, cell[4])), mul_rn(s2, cell[7]));
-                    vec[2] = add_rn(add_rn(add_rn(sub_rn(cur_pt.z, ps[2]), mul_rn(s0, cell[2])),
+                    vec[2] = add_rn(add_rn(add_rn(sub_rn(pt[m].z, ps.z), mul_rn(s0, cell[2])),
                                            mul_rn(s1, cell[5])), mul_rn(s2, cell[8]));
                 }
-                const int64_t s = source + args.index_offset;
-                const int64_t t = target + args.index_offset;
+                const int64_t s = static_cast<int64_t>(ws.w) + args.index_offset;
+                const int64_t t = static_cast<int64_t>(meta[m].w) + args.index_offset;
                 if (wants<Q>(args.out_i, kQ_I)) args.out_i[o] = s;
                 if (wants<Q>(args.out_j, kQ_J)) args.out_j[o] = t;
                 if (wants<Q>(args.out_P, kQ_P)) {
@@ -1093,10 +1174,16 @@ __global__ void __launch_bounds__(kSearchThreads) cell_emit_kernel(SearchArgs<T>
                     row[1] = vec[1];
                     row[2] = vec[2];
                 }
+                }
             }
+            out_row += queued;
+            queued = next_queued;
+            current ^= 1;
         }
+        __syncwarp();
     }
 }
+
 
 // Brute force: one warp per source atom of a brute-force structure (grid-
 // stride over those atoms); lanes stride over the N x I (target, image)
@@ -1368,11 +1455,10 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
     if (write) {
         const int q = (args.out_i ? kQ_I : 0) | (args.out_j ? kQ_J : 0) | (args.out_P ? kQ_P : 0) |
                       (args.out_S ? kQ_S : 0) | (args.out_d ? kQ_d : 0) | (args.out_D ? kQ_D : 0);
-        const int64_t groups = blocks_for((args.n_sources + 31) / 32, kSearchWarps);
-        auto launch = [&](auto kernel, int64_t work) {
-            kernel<<<persistent_blocks(kernel, kSearchThreads, work), kSearchThreads, 0, stream>>>(
-                args);
-    ++g_kernel_launches;
+        const int64_t groups = blocks_for((args.n_sources + 31) / 32, kEmitThreads / 32);
+        auto launch = [&](auto kernel, int64_t work, int threads = kSearchThreads) {
+            kernel<<<persistent_blocks(kernel, threads, work), threads, 0, stream>>>(args);
+            ++g_kernel_launches;
         };
         if (args.source_order == 0) {
             switch (q) {
@@ -1385,12 +1471,12 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
             }
         } else {
             switch (q) {
-                case kQ_P | kQ_S: launch(cell_emit_kernel<T, kQ_P | kQ_S>, groups); break;
+                case kQ_P | kQ_S: launch(cell_emit_kernel<T, kQ_P | kQ_S>, groups, kEmitThreads); break;
                 case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
-                    launch(cell_emit_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>, groups); break;
-                case kQ_P | kQ_S | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_S | kQ_D>, groups); break;
-                case kQ_P | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_D>, groups); break;
-                default: launch(cell_emit_kernel<T, 0>, groups); break;
+                    launch(cell_emit_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>, groups, kEmitThreads); break;
+                case kQ_P | kQ_S | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_S | kQ_D>, groups, kEmitThreads); break;
+                case kQ_P | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_D>, groups, kEmitThreads); break;
+                default: launch(cell_emit_kernel<T, 0>, groups, kEmitThreads); break;
             }
         }
     } else if (args.half_list) {
