@@ -146,6 +146,13 @@ int64_t tnr_last_launch_count(void);
  * Returns the number written (at most 6). */
 int tnr_last_phase_times(float* times_ms, int capacity);
 
+/* Host wall-clock marks (ms since the call began) of the last call on this
+ * host thread when TONARI_B200_PHASE_TIMERS=1 is set, else zeros: metadata
+ * read, geometry built, prepare launched, extents read back, plans uploaded,
+ * ghost totals read back, count pass launched, pair total read back, write
+ * pass launched.  Returns the number written (at most 12). */
+int tnr_last_host_times(double* times_ms, int capacity);
+
 #ifdef __cplusplus
 }
 #endif

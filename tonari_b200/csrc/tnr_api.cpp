@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
 
@@ -57,6 +58,8 @@ constexpr int kRoundoffFactor = 64;
 
 thread_local int64_t g_launches = 0;
 thread_local float g_phase_ms[6] = {0, 0, 0, 0, 0, 0};
+constexpr int kHostMarks = 12;
+thread_local double g_host_ms[kHostMarks] = {};
 
 struct CudaError : std::runtime_error {
     using std::runtime_error::runtime_error;
@@ -199,10 +202,20 @@ struct PhaseTimer {
     cudaStream_t stream = nullptr;
     cudaEvent_t events[7] = {};
     int recorded = 0;
+    std::chrono::steady_clock::time_point start;
+    // Host wall time (ms since the call began) at host mark `index`.
+    void host(int index) {
+        if (enabled && index < kHostMarks) {
+            g_host_ms[index] = std::chrono::duration<double, std::milli>(
+                std::chrono::steady_clock::now() - start).count();
+        }
+    }
     explicit PhaseTimer(cudaStream_t s) : stream(s) {
         const char* flag = std::getenv("TONARI_B200_PHASE_TIMERS");
         enabled = flag && flag[0] == '1';
         for (float& value : g_phase_ms) value = 0.0f;
+        for (double& value : g_host_ms) value = 0.0;
+        start = std::chrono::steady_clock::now();
         if (enabled) {
             for (auto& event : events) cudaEventCreate(&event);
         }
@@ -386,6 +399,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     require_input(batch_ptr[0] == 0, "batch_ptr must start at zero");
     require_input(batch_ptr[batch] == n_atoms, "batch_ptr must end at N_total");
+    timer.host(0);  // metadata on the host
     std::vector<int64_t> counts(static_cast<size_t>(batch));
     for (int64_t b = 0; b < batch; ++b) {
         require_input(batch_ptr[b + 1] >= batch_ptr[b], "batch_ptr must be nondecreasing");
@@ -395,6 +409,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     std::vector<double> cell64(cell_t.begin(), cell_t.end());
     const PeriodicGeometry geometry =
         build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
+    timer.host(1);  // periodic geometry
 
     result.n_pairs = 0;
     if (n_atoms == 0) return;
@@ -447,6 +462,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                                 d_reductions, d_status};
     launch_prepare(prepare_args, stream);
     check_launch("prepare kernel");
+    timer.host(2);  // prepare launched
     timer.mark(1);
 
     // ---- per-structure algorithm ----------------------------------------
@@ -503,6 +519,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         std::memcpy(reductions.data(), pinned_read, reductions.size() * sizeof(Reduction<T>));
         uint32_t status = 0;
         std::memcpy(&status, pinned_read + reductions.size() * sizeof(Reduction<T>), sizeof(status));
+        timer.host(3);  // extents read back
         check_status(status);
         std::vector<CellPlan> outcomes(static_cast<size_t>(batch), CellPlan::kUnsafe);
         HostPool::instance().parallel_for(batch, 256, [&](int64_t begin, int64_t end) {
@@ -554,6 +571,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     const size_t off_brute_structs = second.add(brute_structs.data(), brute_structs.size());
     const size_t off_cell_bins = second.add(cell_bin_prefix.data(), cell_bin_prefix.size());
     char* second_device = second.commit(workspace, stream);
+    timer.host(4);  // plans uploaded
     auto* d_plans = reinterpret_cast<StructurePlan<T>*>(second_device + off_plans);
 
     // ---- cell list binning: histogram -> scan -> scatter ------------------
@@ -626,6 +644,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         check_cuda(cudaStreamSynchronize(stream), "ghost total");
         std::memcpy(&packed_total, pinned_read, sizeof(packed_total));
         std::memcpy(&mask_words, pinned_read + 8, sizeof(mask_words));
+        timer.host(5);  // ghost and mask totals read back
         require_search(mask_words < (1ull << 32), "cell-list candidate bitmask exceeds uint32 indexing");
         d_mask_words = workspace.get<uint32_t>(mask_words);
         const int64_t ghosts = static_cast<int64_t>(packed_total & 0xffffffffull);
@@ -635,7 +654,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                        "cell-list image copies exceed int32 indexing");
         d_ghost_pos = workspace.get<V4>(ghosts);
         d_ghost_meta = workspace.get<int4>(ghosts);
-        d_ghost_orig = workspace.get<V4>(ghosts);
+        if (request.quantities & (TNR_Q_d | TNR_Q_D)) d_ghost_orig = workspace.get<V4>(ghosts);
         d_self_slot = workspace.get<int32_t>(n_atoms);
         d_source_list = workspace.get<int32_t>(n_cell_atoms);
         d_source_bin = workspace.get<int32_t>(n_cell_atoms);
@@ -698,6 +717,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         check_launch("brute count kernel");
     }
     timer.mark(3);
+    timer.host(6);  // count pass launched
     launch_scan_counts(d_counts, n_atoms, d_pair_start, d_scan_workspace, d_status, stream);
     check_launch("pair scan kernel");
     timer.mark(4);
@@ -710,6 +730,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     uint32_t status = 0;
     std::memcpy(&n_pairs, pinned_read, sizeof(n_pairs));
     std::memcpy(&status, pinned_read + sizeof(int64_t), sizeof(status));
+    timer.host(7);  // pair total read back
     check_status(status);
     require_search(n_pairs >= 0, "neighbor-list output exceeds the int64 range");
 
@@ -742,6 +763,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         }
     }
     timer.mark(6);
+    timer.host(8);  // write pass launched
     timer.finish();
 }
 
@@ -814,6 +836,12 @@ int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator
 const char* tnr_version(void) { return "0.1.0"; }
 
 int64_t tnr_last_launch_count(void) { return tnr::g_launches; }
+
+int tnr_last_host_times(double* times_ms, int capacity) {
+    const int count = std::min(capacity, tnr::kHostMarks);
+    for (int k = 0; k < count; ++k) times_ms[k] = tnr::g_host_ms[k];
+    return count;
+}
 
 int tnr_last_phase_times(float* times_ms, int capacity) {
     const int count = std::min(capacity, 6);

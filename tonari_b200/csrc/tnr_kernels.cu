@@ -280,12 +280,14 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
                                                           (k == center ? 1u : 2u)),
                                      T(0));
             reinterpret_cast<V*>(args.ghost_pos)[slot] = record;
-            V original;
-            original.x = args.positions[3 * atom];
-            original.y = args.positions[3 * atom + 1];
-            original.z = args.positions[3 * atom + 2];
-            original.w = index_to_lane(static_cast<int32_t>(atom), T(0));
-            reinterpret_cast<V*>(args.ghost_orig)[slot] = original;
+            if (args.ghost_orig) {  // only the d / D outputs read it
+                V original;
+                original.x = args.positions[3 * atom];
+                original.y = args.positions[3 * atom + 1];
+                original.z = args.positions[3 * atom + 2];
+                original.w = index_to_lane(static_cast<int32_t>(atom), T(0));
+                reinterpret_cast<V*>(args.ghost_orig)[slot] = original;
+            }
             const int4 image = args.image_shift[plan.image_begin + k];
             args.ghost_meta[slot] = make_int4(image.x - wrap[0], image.y - wrap[1],
                                               image.z - wrap[2], static_cast<int32_t>(atom));
@@ -697,10 +699,10 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                         keep = true;
                         if (Half && meta.w == source) keep = canonical_shift(shift);
                         if (keep && !(d2 < inner2)) {
-                            const V pt = reinterpret_cast<const V*>(args.ghost_orig)[slot];
-                            const T vx = exact_component(pt.x, args.positions[3 * source], shift, plan.cell, 0);
-                            const T vy = exact_component(pt.y, args.positions[3 * source + 1], shift, plan.cell, 1);
-                            const T vz = exact_component(pt.z, args.positions[3 * source + 2], shift, plan.cell, 2);
+                            const T* pt = args.positions + 3 * static_cast<int64_t>(meta.w);
+                            const T vx = exact_component(pt[0], args.positions[3 * source], shift, plan.cell, 0);
+                            const T vy = exact_component(pt[1], args.positions[3 * source + 1], shift, plan.cell, 1);
+                            const T vz = exact_component(pt[2], args.positions[3 * source + 2], shift, plan.cell, 2);
                             keep = exact_norm2(vx, vy, vz) < plan.cutoff_squared;
                         }
                         if (keep) keep_bits |= 1u << r;
