@@ -295,7 +295,10 @@ enum class CellPlan { kReady, kUnsafe, kPreferBrute };
 // shifts that could leave int32), with the same pair set.
 template <typename T>
 CellPlan plan_cell(StructurePlan<T>& plan, const Reduction<T>& reduction, const T* cell,
-               double cutoff) {
+               const double* dual, double cutoff) {
+    // Half-list order keys of one structure are compared as signed 32-bit
+    // differences, exact below 2^30 atoms.
+    if (plan.n_atoms >= (int32_t{1} << 30) - 2) return CellPlan::kPreferBrute;
     const T scalar_cutoff = static_cast<T>(cutoff);
     T lo[3], hi[3];
     long double scale = 0.0L;
@@ -361,6 +364,14 @@ CellPlan plan_cell(StructurePlan<T>& plan, const Reduction<T>& reduction, const 
         plan.dims[c] = static_cast<int32_t>(dim);
     }
     plan.search_squared = search * search;
+    // Every nonzero lattice translation is at least as long as the smallest
+    // perpendicular width 1 / |dual column|; only below the search radius
+    // can an atom's own image be its candidate.
+    plan.self_images = 0;
+    for (int a = 0; a < 3; ++a) {
+        const double norm = std::sqrt(dual[a] * dual[a] + dual[3 + a] * dual[3 + a] + dual[6 + a] * dual[6 + a]);
+        if (static_cast<double>(search) * norm * (1.0 + 1e-6) >= 1.0) plan.self_images = 1;
+    }
     plan.inner_squared = inner * inner;
     return CellPlan::kReady;
 }
@@ -525,7 +536,8 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         HostPool::instance().parallel_for(batch, 256, [&](int64_t begin, int64_t end) {
             for (int64_t b = begin; b < end; ++b) {
                 if (mode[b] != kModeCell) continue;
-                outcomes[b] = plan_cell(plans[b], reductions[b], cell_t.data() + 9 * b, request.cutoff);
+                outcomes[b] = plan_cell(plans[b], reductions[b], cell_t.data() + 9 * b,
+                                        geometry.duals.data() + 9 * b, request.cutoff);
             }
         });
         for (int64_t b = 0; b < batch; ++b) {

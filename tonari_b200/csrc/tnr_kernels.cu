@@ -493,13 +493,7 @@ __device__ __forceinline__ unsigned long long distance2_pair(
     return d2;
 }
 
-// The screening distance in scalar form, with explicit roundings so that the
-// rare path re-derives exactly the main test's decisions.
-__device__ __forceinline__ float screen_distance2(float cx, float cy, float cz, float sx, float sy,
-                                                  float sz) {
-    const float dx = __fsub_rn(cx, sx), dy = __fsub_rn(cy, sy), dz = __fsub_rn(cz, sz);
-    return __fmaf_rn(dz, dz, __fmaf_rn(dy, dy, __fmul_rn(dx, dx)));
-}
+// The screening distance in scalar form (double sources in the count pass).
 __device__ __forceinline__ double screen_distance2(double cx, double cy, double cz, double sx,
                                                    double sy, double sz) {
     const double dx = __dsub_rn(cx, sx), dy = __dsub_rn(cy, sy), dz = __dsub_rn(cz, sz);
@@ -526,22 +520,50 @@ __device__ __forceinline__ uint32_t transpose_bits32(uint32_t x, int lane) {
 // sources are staged once in shared memory (up to 32 at a time, structure of
 // arrays) and read back as broadcasts, four per vector load.  Each lane tests
 // its candidate against every source -- for float two sources per packed
-// f32x2 instruction -- and collects one bit per source; a 32 x 32 bit
+// f32x2 instruction -- and shifts the sign bits of d2 - inner2 and
+// d2 - search2 into two words (one funnel shift per test); a 32 x 32 bit
 // transpose across the warp then gives every source its mask word for the
 // tile.  The lanes stay busy whatever the bin's source count.
 //
 // Half lists compare order keys instead of atom indices.  The ghost record's
 // fourth lane carries key 2a + 1 for the zero image of atom a and 2a + 2 for
 // its other images (written by the scatter); a source's key is 2a + 1.
-// Key(c) > key(s) + 1 means atom(c) > atom(s) (accepted by distance alone);
-// key(c) == key(s) + 1 is a periodic image of the source itself (decided by
-// its shift in the rare path); key(c) == key(s) is the zero-shift self pair,
-// which the test neither accepts nor flags and which is set afterwards per
-// include_self.  Full lists accept the self pair by distance (d = 0) and fix
-// it the same way.  Candidates in the band shell are flagged per lane and the
-// flagged lanes re-run their sources to decide them exactly.
+// Key(c) > key(s) + 1 means atom(c) > atom(s) (accepted by distance alone),
+// tested as the sign of (key(s) + 1) - key(c); key(c) == key(s) + 1 is a
+// periodic image of the source itself (decided by its shift in the rare
+// path); key(c) == key(s) is the zero-shift self pair, which the test neither
+// accepts nor flags and which is set afterwards per include_self.
+// Full lists accept the self pair by distance (d = 0) and fix it the same
+// way.  Candidates in the band shell are flagged per lane and the flagged
+// lanes decide them exactly.
 // Accepted-candidate bits are stored transposed -- word w of source rank r at
 // base + w * S + r, S the bin's source count -- one coalesced store per tile.
+
+// Appends the sign bit of `value` to `bits` (bits = bits << 1 | sign).
+__device__ __forceinline__ uint32_t push_sign(uint32_t bits, float value) {
+    return __funnelshift_l(static_cast<uint32_t>(__float_as_int(value)), bits, 1);
+}
+__device__ __forceinline__ uint32_t push_sign(uint32_t bits, double value) {
+    return __funnelshift_l(static_cast<uint32_t>(__double2hiint(value)), bits, 1);
+}
+__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t push_signs2(uint32_t bits, unsigned long long pair) {
+    float lo, hi;
+    unpack2(pair, lo, hi);
+    return push_sign(push_sign(bits, lo), hi);
+}
+
+// Appends bit [key(s) + 1 < key(c)] to `bits`.  Keys of one structure differ
+// by less than 2^31 (fewer than 2^30 atoms), so the signed difference is exact.
+__device__ __forceinline__ uint32_t push_key(uint32_t bits, uint32_t source_key_plus_one,
+                                             uint32_t candidate_key) {
+    return __funnelshift_l(source_key_plus_one - candidate_key, bits, 1);
+}
+
 template <typename T, bool Half>
 __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
@@ -569,12 +591,18 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
         uint32_t* mask = args.mask_words + args.bin_word_start[bin];
         const T search2 = plan.search_squared;
         const T inner2 = plan.inner_squared;
+        unsigned long long inner_pair = 0, search_pair = 0;
+        if constexpr (std::is_same<T, float>::value) {
+            inner_pair = pack2(inner2, inner2);
+            search_pair = pack2(search2, search2);
+        }
 
         for (uint32_t base = 0; base < n_sources; base += 32) {
             const int block = static_cast<int>(min(32u, n_sources - base));
-            // Sources are padded to a multiple of four with NaN positions,
-            // which no candidate is ever accepted for or in the band of.
+            // Sources are padded to a multiple of four with NaN positions;
+            // their bits are masked off below.
             const int padded = (block + 3) & ~3;
+            const uint32_t valid_mask = block == 32 ? kFullMask : (1u << block) - 1u;
             int32_t my_source = -1;
             int32_t self_k = -1;  // candidate index of my source's zero image
             __syncwarp();
@@ -584,7 +612,8 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 source_x[warp][lane] = q.x;
                 source_y[warp][lane] = q.y;
                 source_z[warp][lane] = q.z;
-                source_key[warp][lane] = Half ? 2u * static_cast<uint32_t>(my_source) + 1u
+                // Half lists: key(s) + 1; full lists: the atom.
+                source_key[warp][lane] = Half ? 2u * static_cast<uint32_t>(my_source) + 2u
                                               : static_cast<uint32_t>(my_source);
                 const int32_t self = args.self_slot[my_source];
 #pragma unroll
@@ -629,76 +658,71 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 const V cand = next;
                 const int32_t slot = next_slot;
                 if (w + 1 < words) load_candidate(w + 1, next, next_slot);
-                const uint32_t cand_key = static_cast<uint32_t>(lane_to_index(cand.w));
-                uint32_t key = 0, key_less = 0;  // key(c) and key(c) - 1
-                unsigned long long cx = 0, cy = 0, cz = 0;
+                const uint32_t key = static_cast<uint32_t>(lane_to_index(cand.w));
+                uint32_t key_signs = 0;  // half lists: bit r = key(s_r) + 1 < key(c)
+                uint32_t inner_signs = 0, search_signs = 0;
                 if constexpr (std::is_same<T, float>::value) {
-                    cx = pack2(cand.x, cand.x);
-                    cy = pack2(cand.y, cand.y);
-                    cz = pack2(cand.z, cand.z);
-                }
-                if constexpr (Half) {
-                    key = cand_key;  // 0 for an empty lane
-                    key_less = key - 1u;
-                }
-                // Bit r of keep_bits: this lane's candidate is accepted for
-                // source r.  rare: some source has it in its band.
-                uint32_t keep_bits = 0;
-                bool rare = false;
-                for (int r0 = 0; r0 < padded; r0 += 4) {
-                    T d2[4];
-                    if constexpr (std::is_same<T, float>::value) {
+                    const unsigned long long cx = pack2(cand.x, cand.x);
+                    const unsigned long long cy = pack2(cand.y, cand.y);
+                    const unsigned long long cz = pack2(cand.z, cand.z);
+                    for (int r0 = 0; r0 < padded; r0 += 4) {
                         const ulonglong2 sx = *reinterpret_cast<const ulonglong2*>(&source_x[warp][r0]);
                         const ulonglong2 sy = *reinterpret_cast<const ulonglong2*>(&source_y[warp][r0]);
                         const ulonglong2 sz = *reinterpret_cast<const ulonglong2*>(&source_z[warp][r0]);
-                        unpack2(distance2_pair(cx, cy, cz, sx.x, sy.x, sz.x), d2[0], d2[1]);
-                        unpack2(distance2_pair(cx, cy, cz, sx.y, sy.y, sz.y), d2[2], d2[3]);
-                    } else {
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            d2[u] = screen_distance2(cand.x, cand.y, cand.z, source_x[warp][r0 + u],
-                                                     source_y[warp][r0 + u], source_z[warp][r0 + u]);
-                        }
-                    }
-                    const uint4 keys = *reinterpret_cast<const uint4*>(&source_key[warp][r0]);
-                    const uint32_t key_of[4] = {keys.x, keys.y, keys.z, keys.w};
-                    uint32_t nibble = 0;
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        bool keep = d2[u] < inner2;
-                        bool band = d2[u] < search2;
+                        const unsigned long long d01 = distance2_pair(cx, cy, cz, sx.x, sy.x, sz.x);
+                        const unsigned long long d23 = distance2_pair(cx, cy, cz, sx.y, sy.y, sz.y);
+                        inner_signs = push_signs2(push_signs2(inner_signs, sub2(d01, inner_pair)),
+                                                  sub2(d23, inner_pair));
+                        search_signs = push_signs2(push_signs2(search_signs, sub2(d01, search_pair)),
+                                                   sub2(d23, search_pair));
                         if constexpr (Half) {
-                            keep = keep && key_less > key_of[u];
-                            band = band && key > key_of[u];
+                            const uint4 k = *reinterpret_cast<const uint4*>(&source_key[warp][r0]);
+                            key_signs = push_key(push_key(push_key(push_key(key_signs, k.x, key), k.y, key),
+                                                          k.z, key), k.w, key);
                         }
-                        if (keep) nibble |= 1u << u;
-                        rare = rare | (band & !keep);
                     }
-                    keep_bits |= nibble << r0;
-                }
-                if (__any_sync(kFullMask, rare) && rare) {
-                    // Rare: band shell, or a half-list periodic image of the
-                    // source itself; decided exactly by the candidate's lane.
-                    for (int r = 0; r < block; ++r) {
+                } else {
+                    for (int r = 0; r < padded; ++r) {
                         const T d2 = screen_distance2(cand.x, cand.y, cand.z, source_x[warp][r],
                                                       source_y[warp][r], source_z[warp][r]);
-                        const uint32_t key_r = source_key[warp][r];
-                        bool keep = d2 < inner2;
-                        bool band = d2 < search2;
-                        if constexpr (Half) {
-                            keep = keep && key_less > key_r;
-                            band = band && key > key_r;
+                        inner_signs = push_sign(inner_signs, d2 - inner2);
+                        search_signs = push_sign(search_signs, d2 - search2);
+                        if constexpr (Half) key_signs = push_key(key_signs, source_key[warp][r], key);
+                    }
+                }
+                // Bit r: d2 to source r below the inner / search radius.
+                const uint32_t inside = __brev(inner_signs) >> (32 - padded);
+                const uint32_t near = __brev(search_signs) >> (32 - padded);
+                uint32_t keep_keys = valid_mask, band_keys = valid_mask;
+                if constexpr (Half) {
+                    keep_keys = band_keys = (__brev(key_signs) >> (32 - padded)) & valid_mask;
+                    // key(c) == key(s) + 1: an image of source s itself, only
+                    // possible where a lattice translation is shorter than the
+                    // search radius; its shift decides it in the rare path.
+                    if (plan.self_images && (key & 1u) == 0u && key != 0u) {
+                        for (int r = 0; r < block; ++r) {
+                            if (source_key[warp][r] == key) band_keys |= 1u << r;
                         }
-                        if (!band || keep) continue;
-                        const int32_t source = static_cast<int32_t>(Half ? key_r >> 1 : key_r);
-                        const int4 meta = args.ghost_meta[slot];  // .w: the candidate's atom
+                    }
+                }
+                uint32_t keep_bits = inside & keep_keys;
+                uint32_t rare = near & band_keys & ~keep_bits;
+                if (__any_sync(kFullMask, rare != 0u) && rare != 0u) {
+                    // Rare: band shell, or a half-list periodic image of the
+                    // source itself; decided exactly by the candidate's lane.
+                    const int4 meta = args.ghost_meta[slot];  // .w: the candidate's atom
+                    do {
+                        const int r = __ffs(rare) - 1;
+                        rare &= rare - 1u;
+                        const uint32_t key_r = source_key[warp][r];
+                        const int32_t source = static_cast<int32_t>(Half ? (key_r - 2u) >> 1 : key_r);
                         const long long shift[3] = {
                             meta.x + static_cast<long long>(args.wraps[3 * source]),
                             meta.y + static_cast<long long>(args.wraps[3 * source + 1]),
                             meta.z + static_cast<long long>(args.wraps[3 * source + 2])};
-                        keep = true;
+                        bool keep = true;
                         if (Half && meta.w == source) keep = canonical_shift(shift);
-                        if (keep && !(d2 < inner2)) {
+                        if (keep && !((inside >> r) & 1u)) {
                             const T* pt = args.positions + 3 * static_cast<int64_t>(meta.w);
                             const T vx = exact_component(pt[0], args.positions[3 * source], shift, plan.cell, 0);
                             const T vy = exact_component(pt[1], args.positions[3 * source + 1], shift, plan.cell, 1);
@@ -706,7 +730,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                             keep = exact_norm2(vx, vy, vz) < plan.cutoff_squared;
                         }
                         if (keep) keep_bits |= 1u << r;
-                    }
+                    } while (rare != 0u);
                 }
                 // Transpose the warp's 32 x 32 bit matrix: afterwards lane r
                 // holds source r's word (bit c = candidate lane c accepted).

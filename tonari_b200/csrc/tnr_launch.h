@@ -56,7 +56,7 @@ struct SearchArgs {
     const void* ghost_pos;  // vec4_t<T>
     const int4* ghost_meta;
     const int32_t* self_slot;
-    const int32_t* source_list;
+    int32_t* source_list;               // cell order; the count pass sorts each bin's 32-source blocks
     const int32_t* source_bin;          // [sources] bin of each source, cell order
     int64_t n_sources;
     const int32_t* bin_struct;          // [bins] structure of each bin

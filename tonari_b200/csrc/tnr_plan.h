@@ -77,7 +77,7 @@ struct StructurePlan {
     int32_t repeats[3];
     int64_t bin_begin;     // first bin of this structure (cell mode)
     int32_t dims[3];       // bins per axis (cell mode)
-    int32_t pad0;
+    int32_t self_images;   // a nonzero lattice translation may be shorter than the search radius
     T cell[9];
     T origin[3];           // lower corner of the bin grid
     T inv_edge;            // 1 / bin edge
