@@ -221,3 +221,34 @@ def test_fused_displacement_gradients_match_reference_formula(dtype):
     tol = 1e-4 if dtype == torch.float32 else 1e-10
     torch.testing.assert_close(pos_a.grad, pos_b.grad, rtol=tol, atol=tol)
     torch.testing.assert_close(cell_a.grad, cell_b.grad, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("half_list", [False, True])
+@pytest.mark.parametrize("sorted_output", [False, True])
+def test_cell_list_small_cells_own_images(dtype, half_list, sorted_output):
+    # Cells shorter than the cutoff: atoms pair with their own periodic
+    # images, which half lists keep by the canonical shift rule
+    # (tests/backends/test_pair_identity.py:13-81 for the rule).
+    generator = torch.Generator().manual_seed(7021)
+    cells, blocks, counts = [], [], (40, 3, 65)
+    for k, n in enumerate(counts):
+        cell = torch.diag(2.6 + 1.2 * torch.rand(3, generator=generator, dtype=dtype))
+        cell += 0.4 * torch.tril(torch.rand((3, 3), generator=generator, dtype=dtype), diagonal=-1)
+        cells.append(cell)
+        blocks.append(torch.rand((n, 3), generator=generator, dtype=dtype) @ cell)
+    positions = torch.cat(blocks)
+    cell = torch.stack(cells)
+    pbc = torch.tensor([[True, True, True], [True, False, True], [True, True, True]])
+    batch_ptr = torch.tensor([0, counts[0], counts[0] + counts[1], sum(counts)])
+    pairs, shifts, D = run(positions, cell, pbc, 4.0, batch_ptr, quantities="PSD",
+                           algorithm="cell_list", half_list=half_list, sorted=sorted_output)
+    if sorted_output:
+        assert_sorted_by_source(pairs)
+    assert_same_pairs(pairs, shifts, *expected_pairs(positions, cell, pbc, 4.0, batch_ptr,
+                                                     half_list=half_list))
+    P, S = pairs.cpu().numpy(), shifts.cpu().numpy()
+    ref_D = oracle.public_displacements(positions.numpy(), cell.numpy(), batch_ptr.numpy(), P, S)
+    scale = np.maximum(np.linalg.norm(ref_D.astype(np.float64), axis=1), 4e-3)
+    err = np.linalg.norm(D.cpu().numpy().astype(np.float64) - ref_D, axis=1)
+    assert np.all(err <= TOLERANCE[dtype] * scale * 4)
