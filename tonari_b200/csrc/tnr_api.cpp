@@ -498,8 +498,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                        "atom representatives require periodic wraps outside the int32 range");
         require_search(!(status & kStatusShiftRange),
                        "a cell shift required by the cutoff pairs exceeds the int32 output range");
-        require_search(!(status & kStatusScanTimeout),
-                       "a device-wide scan exceeded its bounded wait");
         require_search(!(status & kStatusCapacity), "an internal capacity was exceeded");
         require_search(!(status & kStatusCountRange),
                        "a per-source pair count exceeds the int32 range");

@@ -6,7 +6,7 @@
 //   bin       per cell-list atom x image: cull the image copy against the
 //             structure's box, histogram it into a Cartesian bin (pass 1) or
 //             scatter it into cell-sorted order (pass 2)
-//   scan      decoupled look-back exclusive scans (tnr_scan.cuh)
+//   scan      three-launch exclusive scans (tnr_scan.cuh)
 //   search    one warp per source atom: walk the 3x3 rows of the 27-bin
 //             stencil as one flattened candidate range (cell list) or every
 //             (target, image) candidate (brute force); count pass, then write
@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(kPrepareThreads) prepare_kernel(PrepareArgs<T>
         block_first_last[0] = structure_of(args.batch_ptr, args.batch, block_base);
         block_first_last[1] = structure_of(args.batch_ptr, args.batch, last);
     }
+    __syncthreads();
 
     Extents<K> ext;
 #pragma unroll
@@ -143,7 +144,8 @@ __global__ void __launch_bounds__(kPrepareThreads) prepare_kernel(PrepareArgs<T>
     }
     int32_t sid = -1;
     if (valid) {
-        sid = structure_of(args.batch_ptr, args.batch, atom);
+        sid = structure_of(args.batch_ptr, args.batch, atom, block_first_last[0],
+                           block_first_last[1] + 1);
         args.atom_struct[atom] = sid;
         const PrepareStructure<T>& st = args.structures[sid];
         const T p[3] = {args.positions[3 * atom], args.positions[3 * atom + 1],
@@ -240,9 +242,18 @@ __global__ void __launch_bounds__(kPrepareThreads) prepare_kernel(PrepareArgs<T>
 template <typename T, bool Scatter>
 __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
     using V = vec4_t<T>;
-    const int64_t index = static_cast<int64_t>(blockIdx.x) * kBinThreads + threadIdx.x;
+    __shared__ int32_t block_first_last[2];
+    const int64_t block_base = static_cast<int64_t>(blockIdx.x) * kBinThreads;
+    const int64_t index = block_base + threadIdx.x;
+    if (threadIdx.x == 0) {
+        const int64_t last = min(args.n_cell_atoms - 1, block_base + kBinThreads - 1);
+        block_first_last[0] = segment_of(args.cell_prefix, args.n_cell, block_base);
+        block_first_last[1] = segment_of(args.cell_prefix, args.n_cell, last);
+    }
+    __syncthreads();
     if (index >= args.n_cell_atoms) return;
-    const int32_t c = segment_of(args.cell_prefix, args.n_cell, index);
+    const int32_t c = segment_of(args.cell_prefix, args.n_cell, index, block_first_last[0],
+                                 block_first_last[1] + 1);
     const StructurePlan<T>& plan = args.plans[args.cell_structs[c]];
     const int64_t atom = plan.atom_begin + (index - args.cell_prefix[c]);
     const V q = reinterpret_cast<const V*>(args.wrapped)[atom];
@@ -445,27 +456,35 @@ __device__ __forceinline__ int32_t slot_of(const StencilRows& rows, int32_t k) {
 
 
 // Per bin: bitmask words of all its sources (sources * ceil(candidates / 32)).
+// One thread per bin; its 18 row-bound loads are independent.
 template <typename T>
 __global__ void __launch_bounds__(kBinThreads) stencil_words_kernel(SearchArgs<T> args,
                                                                     int64_t n_bins,
                                                                     unsigned long long* bin_words) {
-    const int lane = threadIdx.x & 31;
-    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t bin = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-         bin < n_bins; bin += stride) {
-        const unsigned long long sources =
-            (args.bin_start[bin + 1] >> 32) - (args.bin_start[bin] >> 32);
-        if (sources == 0) {
-            if (lane == 0) bin_words[bin] = 0;
-            continue;
-        }
-        const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
-        int32_t bx, by, bz;
-        bin_coordinates(plan, bin, bx, by, bz);
-        const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz,
-                                           static_cast<StencilRows*>(nullptr), lane);
-        if (lane == 0) bin_words[bin] = sources * static_cast<unsigned long long>((total + 31) >> 5);
+    const int64_t bin = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (bin >= n_bins) return;
+    const unsigned long long sources = (args.bin_start[bin + 1] >> 32) - (args.bin_start[bin] >> 32);
+    if (sources == 0) {
+        bin_words[bin] = 0;
+        return;
     }
+    const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
+    int32_t bx, by, bz;
+    bin_coordinates(plan, bin, bx, by, bz);
+    const int32_t z0 = max(bz - 1, 0);
+    const int32_t z1 = min(bz + 1, plan.dims[2] - 1);
+    int64_t total = 0;
+#pragma unroll
+    for (int r = 0; r < 9; ++r) {
+        const int32_t x = bx + r / 3 - 1;
+        const int32_t y = by + r % 3 - 1;
+        if (x >= 0 && x < plan.dims[0] && y >= 0 && y < plan.dims[1]) {
+            const int64_t row = plan.bin_begin + (static_cast<int64_t>(x) * plan.dims[1] + y) * plan.dims[2];
+            total += static_cast<int64_t>(args.bin_start[row + z1 + 1] & 0xffffffffull) -
+                     static_cast<int64_t>(args.bin_start[row + z0] & 0xffffffffull);
+        }
+    }
+    bin_words[bin] = sources * static_cast<unsigned long long>((total + 31) >> 5);
 }
 
 // Packed pairs of floats (sm_100 f32x2 arithmetic): two source-candidate
@@ -1468,8 +1487,7 @@ template <typename T>
 void launch_stencil_words(const SearchArgs<T>& args, unsigned long long* bin_words,
                           cudaStream_t stream) {
     if (args.n_bins == 0) return;
-    const unsigned blocks = persistent_blocks(stencil_words_kernel<T>, kBinThreads,
-                                              blocks_for(args.n_bins, kBinThreads / 32));
+    const unsigned blocks = static_cast<unsigned>(blocks_for(args.n_bins, kBinThreads));
     stencil_words_kernel<T><<<blocks, kBinThreads, 0, stream>>>(args, args.n_bins, bin_words);
     ++g_kernel_launches;
 }
@@ -1535,42 +1553,34 @@ void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t str
 
 size_t scan_workspace_bytes(int64_t n) {
     const int64_t tiles = std::max<int64_t>(1, (n + kScanTile - 1) / kScanTile);
-    // counter + flags, then 8-byte aligned aggregate and inclusive arrays.
-    const size_t words = static_cast<size_t>(1 + tiles);
-    const size_t head = (words * sizeof(uint32_t) + 15) / 16 * 16;
-    return head + 2 * static_cast<size_t>(tiles) * sizeof(int64_t);
+    return static_cast<size_t>(tiles) * sizeof(int64_t);
 }
 
 namespace {
 template <typename In, typename Out>
-void launch_scan(const In* in, int64_t n, Out* out, Out* out2, void* workspace,
-                 uint32_t* status, cudaStream_t stream) {
+void launch_scan(const In* in, int64_t n, Out* out, Out* out2, void* workspace, cudaStream_t stream) {
     const int64_t tiles = std::max<int64_t>(1, (n + kScanTile - 1) / kScanTile);
-    const size_t words = static_cast<size_t>(1 + tiles);
-    const size_t head = (words * sizeof(uint32_t) + 15) / 16 * 16;
-    char* bytes = static_cast<char*>(workspace);
-    cudaMemsetAsync(bytes, 0, words * sizeof(uint32_t), stream);
-    ScanTileState<Out> state;
-    state.counter = reinterpret_cast<uint32_t*>(bytes);
-    state.flags = state.counter + 1;
-    state.aggregate = reinterpret_cast<Out*>(bytes + head);
-    state.inclusive = state.aggregate + tiles;
-    exclusive_scan_kernel<In, Out><<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
-        in, n, out, out2, state, status);
-    ++g_kernel_launches;
+    Out* tile_sums = static_cast<Out*>(workspace);
+    scan_reduce_kernel<In, Out><<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
+        in, n, tile_sums);
+    scan_tiles_kernel<Out><<<1, kScanTilesThreads, 0, stream>>>(tile_sums, tiles);
+    scan_apply_kernel<In, Out><<<static_cast<unsigned>(tiles), kScanThreads, 0, stream>>>(
+        in, n, tile_sums, out, out2);
+    g_kernel_launches += 3;
 }
 }  // namespace
 
 void launch_scan_u64(const unsigned long long* in, int64_t n, unsigned long long* out,
                      unsigned long long* out2, void* workspace, uint32_t* status,
                      cudaStream_t stream) {
-    launch_scan<unsigned long long, unsigned long long>(in, n, out, out2, workspace, status,
-                                                        stream);
+    (void)status;
+    launch_scan<unsigned long long, unsigned long long>(in, n, out, out2, workspace, stream);
 }
 
 void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* workspace,
                         uint32_t* status, cudaStream_t stream) {
-    launch_scan<uint32_t, int64_t>(in, n, out, nullptr, workspace, status, stream);
+    (void)status;
+    launch_scan<uint32_t, int64_t>(in, n, out, nullptr, workspace, stream);
 }
 
 #define TNR_INSTANTIATE(T)                                                                 \

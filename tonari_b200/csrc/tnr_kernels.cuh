@@ -117,9 +117,11 @@ __device__ __forceinline__ int32_t bin_axis(T value, T origin, T inv_edge, int32
 
 // Index of the structure containing `atom`: the b with
 // batch_ptr[b] <= atom < batch_ptr[b+1] (skipping empty structures).
+// The search may be narrowed to [lo, hi) when the answer is known to be there.
 __device__ __forceinline__ int32_t structure_of(const int64_t* __restrict__ batch_ptr,
-                                                int64_t batch, int64_t atom) {
-    int64_t lo = 0, hi = batch;  // answer in [0, batch)
+                                                int64_t batch, int64_t atom, int64_t lo = 0,
+                                                int64_t hi = -1) {
+    if (hi < 0) hi = batch;  // answer in [lo, hi)
     while (hi - lo > 1) {
         const int64_t mid = (lo + hi) >> 1;
         if (batch_ptr[mid] <= atom) lo = mid; else hi = mid;
@@ -129,9 +131,10 @@ __device__ __forceinline__ int32_t structure_of(const int64_t* __restrict__ batc
 
 // Position of `value` in a nondecreasing prefix array of length count+1:
 // the k with prefix[k] <= value < prefix[k+1].
+// The search may be narrowed to [lo, hi) when the answer is known to be there.
 __device__ __forceinline__ int32_t segment_of(const int64_t* __restrict__ prefix, int32_t count,
-                                              int64_t value) {
-    int32_t lo = 0, hi = count;
+                                              int64_t value, int32_t lo = 0, int32_t hi = -1) {
+    if (hi < 0) hi = count;
     while (hi - lo > 1) {
         const int32_t mid = (lo + hi) >> 1;
         if (prefix[mid] <= value) lo = mid; else hi = mid;

@@ -118,8 +118,9 @@ void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t str
 // Running count of kernels this host thread has launched through this file.
 int64_t launched_kernels();
 
-// Exclusive scans (n+1 outputs).  `tile_words` is workspace of
-// scan_workspace_bytes(n) bytes; it is cleared inside.
+// Exclusive scans (n+1 outputs), three launches each.  `workspace` holds
+// scan_workspace_bytes(n) bytes of per-tile sums.  `status` is unused: no
+// CTA of the scan waits on another.
 size_t scan_workspace_bytes(int64_t n);
 void launch_scan_u64(const unsigned long long* in, int64_t n, unsigned long long* out,
                      unsigned long long* out2, void* workspace, uint32_t* status,

@@ -30,7 +30,7 @@ enum StatusBit : uint32_t {
     kStatusNonFinite = 1u << 0,     // "positions must contain only finite values"
     kStatusWrapRange = 1u << 1,     // wraps outside int32
     kStatusShiftRange = 1u << 2,    // accepted pair's shift outside int32
-    kStatusScanTimeout = 1u << 3,   // a bounded look-back wait gave up
+    kStatusReserved3 = 1u << 3,     // unused (no kernel waits on another)
     kStatusCapacity = 1u << 4,      // an internal capacity was exceeded
     kStatusCountRange = 1u << 5     // a per-source count overflowed int32
 };

@@ -1,14 +1,12 @@
-// Single-pass exclusive prefix sum with decoupled look-back.
+// Exclusive prefix sum in three launches: per-tile sums, a one-block scan of
+// the tile sums, and a pass that rescans each tile from its prefix.
 //
 // Replaces the reference's torch::cumsum calls (tonari
 // csrc/torch/neighbors_cell_cuda.cu:641-656 and :775-777), which are a
-// library scan followed by a host round trip.  Each CTA claims a tile id in
-// launch order (so every predecessor it waits on is already resident), scans
-// its tile in registers and shared memory, publishes its aggregate, and then
-// one thread walks back over predecessor tiles until it meets an inclusive
-// prefix.  Every wait is bounded: after kScanSpinLimit polls the tile gives
-// up, raises kStatusScanTimeout in the status word and carries on with the
-// partial prefix, so a failure surfaces as a host error instead of a hang.
+// library scan followed by a host round trip.  No CTA waits on another, so
+// the scan needs no spin loop; the input is read twice (it is small: one
+// word per atom or per bin), every load and store is coalesced (lane-
+// contiguous within a warp), and a tile of kScanTile items is one CTA.
 //
 // out has n + 1 entries: out[k] = sum(in[0:k]), out[n] = total.  When out2 is
 // non-null the same values are written there as well (used to initialise the
@@ -22,17 +20,9 @@
 namespace tnr {
 
 constexpr int kScanThreads = 256;
-constexpr int kScanItems = 8;
+constexpr int kScanItems = 16;  // per thread
 constexpr int kScanTile = kScanThreads * kScanItems;
-constexpr uint32_t kScanSpinLimit = 1u << 22;
-
-template <typename Out>
-struct ScanTileState {
-    uint32_t* counter;  // 1 word, zeroed before launch
-    uint32_t* flags;    // [tiles], zeroed before launch: 0 none, 1 aggregate, 2 inclusive
-    Out* aggregate;     // [tiles]
-    Out* inclusive;     // [tiles]
-};
+constexpr int kScanTilesThreads = 1024;
 
 template <typename Out>
 __device__ __forceinline__ Out warp_inclusive_sum(Out value) {
@@ -45,98 +35,110 @@ __device__ __forceinline__ Out warp_inclusive_sum(Out value) {
     return value;
 }
 
-template <typename In, typename Out>
-__global__ void __launch_bounds__(kScanThreads)
-exclusive_scan_kernel(const In* __restrict__ in, int64_t n, Out* __restrict__ out,
-                      Out* __restrict__ out2, ScanTileState<Out> state, uint32_t* status) {
-    __shared__ uint32_t tile_shared;
-    __shared__ Out warp_totals[kScanThreads / 32];
-    __shared__ Out tile_prefix_shared;
-    if (threadIdx.x == 0) tile_shared = atomicAdd(state.counter, 1u);
-    __syncthreads();
-    const uint32_t tile = tile_shared;
-    const int64_t base = static_cast<int64_t>(tile) * kScanTile;
-
-    // Blocked load: thread t owns items [t*kScanItems, (t+1)*kScanItems).
-    Out items[kScanItems];
-    Out thread_sum = 0;
-#pragma unroll
-    for (int k = 0; k < kScanItems; ++k) {
-        const int64_t index = base + threadIdx.x * kScanItems + k;
-        items[k] = index < n ? static_cast<Out>(in[index]) : Out(0);
-        thread_sum += items[k];
-    }
+// Block-wide sum; every thread receives the total.
+template <typename Out, int Threads>
+__device__ __forceinline__ Out block_sum(Out value, Out* warp_shared) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const Out warp_inclusive = warp_inclusive_sum(thread_sum);
-    if (lane == 31) warp_totals[warp] = warp_inclusive;
-    __syncthreads();
-    if (warp == 0) {
-        Out total = lane < kScanThreads / 32 ? warp_totals[lane] : Out(0);
-        total = warp_inclusive_sum(total);
-        if (lane < kScanThreads / 32) warp_totals[lane] = total;  // inclusive per warp
-    }
-    __syncthreads();
-    const Out tile_total = warp_totals[kScanThreads / 32 - 1];
-
-    if (threadIdx.x == 0) {
-        Out prefix = 0;
-        volatile uint32_t* flags = state.flags;
-        if (tile == 0) {
-            state.inclusive[0] = tile_total;
-            __threadfence();
-            flags[0] = 2u;
-        } else {
-            state.aggregate[tile] = tile_total;
-            __threadfence();
-            flags[tile] = 1u;
-            int64_t predecessor = static_cast<int64_t>(tile) - 1;
-            uint32_t spins = 0;
-            while (predecessor >= 0) {
-                const uint32_t flag = flags[predecessor];
-                if (flag == 0u) {
-                    if (++spins > kScanSpinLimit) {
-                        atomicOr(status, static_cast<uint32_t>(kStatusScanTimeout));
-                        break;
-                    }
-                    __nanosleep(32);
-                    continue;
-                }
-                __threadfence();
-                if (flag == 2u) {
-                    prefix += *reinterpret_cast<volatile Out*>(&state.inclusive[predecessor]);
-                    break;
-                }
-                prefix += *reinterpret_cast<volatile Out*>(&state.aggregate[predecessor]);
-                --predecessor;
-            }
-            state.inclusive[tile] = prefix + tile_total;
-            __threadfence();
-            flags[tile] = 2u;
-        }
-        tile_prefix_shared = prefix;
-    }
-    __syncthreads();
-    Out running = tile_prefix_shared + (warp > 0 ? warp_totals[warp - 1] : Out(0)) +
-                  (warp_inclusive - thread_sum);
 #pragma unroll
-    for (int k = 0; k < kScanItems; ++k) {
-        const int64_t index = base + threadIdx.x * kScanItems + k;
-        if (index < n) {
-            out[index] = running;
-            if (out2) out2[index] = running;
-        }
-        running += items[k];
+    for (int offset = 16; offset > 0; offset >>= 1) value += __shfl_xor_sync(0xffffffffu, value, offset);
+    if (lane == 0) warp_shared[warp] = value;
+    __syncthreads();
+    Out total = 0;
+#pragma unroll
+    for (int w = 0; w < Threads / 32; ++w) total += warp_shared[w];
+    __syncthreads();
+    return total;
+}
+
+// Pass 1: tile_sums[t] = sum of tile t.  Thread k of a warp reads items
+// warp_base + 32 * i + k, so each load instruction is one contiguous run.
+template <typename In, typename Out>
+__global__ void __launch_bounds__(kScanThreads)
+scan_reduce_kernel(const In* __restrict__ in, int64_t n, Out* __restrict__ tile_sums) {
+    __shared__ Out warp_shared[kScanThreads / 32];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile + warp * (32 * kScanItems);
+    Out sum = 0;
+#pragma unroll
+    for (int i = 0; i < kScanItems; ++i) {
+        const int64_t index = base + 32 * i + lane;
+        if (index < n) sum += static_cast<Out>(in[index]);
     }
-    // The tile holding the last element also writes the grand total.
-    const int64_t last = n - 1;
-    if (n == 0) {
-        if (tile == 0 && threadIdx.x == 0) {
-            out[0] = 0;
-            if (out2) out2[0] = 0;
+    const Out total = block_sum<Out, kScanThreads>(sum, warp_shared);
+    if (threadIdx.x == 0) tile_sums[blockIdx.x] = total;
+}
+
+// Pass 2 (one CTA): tile_sums becomes its exclusive scan, in place.
+template <typename Out>
+__global__ void __launch_bounds__(kScanTilesThreads)
+scan_tiles_kernel(Out* __restrict__ tile_sums, int64_t tiles) {
+    __shared__ Out warp_shared[kScanTilesThreads / 32];
+    __shared__ Out carry_shared;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    Out carry = 0;
+    for (int64_t chunk = 0; chunk < tiles; chunk += kScanTilesThreads) {
+        const int64_t index = chunk + threadIdx.x;
+        const Out value = index < tiles ? tile_sums[index] : Out(0);
+        const Out inclusive = warp_inclusive_sum(value);
+        if (lane == 31) warp_shared[warp] = inclusive;
+        __syncthreads();
+        if (warp == 0) {
+            const Out w = warp_shared[lane];
+            const Out w_inclusive = warp_inclusive_sum(w);
+            warp_shared[lane] = w_inclusive - w;  // exclusive per warp
+            if (lane == 31) carry_shared = w_inclusive;
         }
-    } else if (last >= base + threadIdx.x * kScanItems &&
-               last < base + (threadIdx.x + 1) * kScanItems) {
+        __syncthreads();
+        if (index < tiles) tile_sums[index] = carry + warp_shared[warp] + inclusive - value;
+        carry += carry_shared;
+        __syncthreads();
+    }
+}
+
+// Pass 3: every tile rescans its items from its prefix and writes out (and
+// out2); the tile holding the last item also writes out[n].
+template <typename In, typename Out>
+__global__ void __launch_bounds__(kScanThreads)
+scan_apply_kernel(const In* __restrict__ in, int64_t n, const Out* __restrict__ tile_prefix,
+                  Out* __restrict__ out, Out* __restrict__ out2) {
+    __shared__ Out warp_shared[kScanThreads / 32];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile + warp * (32 * kScanItems);
+    Out values[kScanItems];
+    Out sum = 0;
+#pragma unroll
+    for (int i = 0; i < kScanItems; ++i) {
+        const int64_t index = base + 32 * i + lane;
+        values[i] = index < n ? static_cast<Out>(in[index]) : Out(0);
+        sum += values[i];
+    }
+    // This warp's total, then the prefix of the warps before it.
+    Out warp_total = sum;
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) {
+        warp_total += __shfl_xor_sync(0xffffffffu, warp_total, offset);
+    }
+    if (lane == 0) warp_shared[warp] = warp_total;
+    __syncthreads();
+    Out running = tile_prefix[blockIdx.x];
+    for (int w = 0; w < warp; ++w) running += warp_shared[w];
+#pragma unroll
+    for (int i = 0; i < kScanItems; ++i) {
+        const Out inclusive = warp_inclusive_sum(values[i]);
+        const int64_t index = base + 32 * i + lane;
+        if (index < n) {
+            out[index] = running + inclusive - values[i];
+            if (out2) out2[index] = running + inclusive - values[i];
+        }
+        running += __shfl_sync(0xffffffffu, inclusive, 31);
+    }
+    const int64_t last_tile = n == 0 ? 0 : (n - 1) / kScanTile;
+    if (blockIdx.x == last_tile && threadIdx.x == kScanThreads - 1) {
+        // The last warp's running value is the grand total.
         out[n] = running;
         if (out2) out2[n] = running;
     }

@@ -257,7 +257,7 @@ void run_static(const tnr_request& request, cudaStream_t stream, int64_t capacit
                    "atom representatives require periodic wraps outside the int32 range");
     require_search(!(status & kStatusShiftRange),
                    "a cell shift required by the cutoff pairs exceeds the int32 output range");
-    require_search(!(status & (kStatusScanTimeout | kStatusCapacity | kStatusCountRange)),
+    require_search(!(status & (kStatusCapacity | kStatusCountRange)),
                    "the static neighbor-list search failed an internal check");
     result.n_pairs = n_pairs;
     if (n_pairs > capacity) {
