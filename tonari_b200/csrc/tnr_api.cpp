@@ -184,6 +184,17 @@ public:
         size_ = offset + std::max<size_t>(bytes, 1);
         return offset;
     }
+    // Reserves room for `count` items to be written in place (no copy).
+    template <typename U>
+    U* place(size_t count, size_t& offset) {
+        offset = add<U>(nullptr, 0);
+        const size_t bytes = count * sizeof(U);
+        if (offset + std::max<size_t>(bytes, 1) > capacity_) {
+            throw std::runtime_error("internal error: upload staging overflow");
+        }
+        size_ = offset + std::max<size_t>(bytes, 1);
+        return reinterpret_cast<U*>(pinned_ + offset);
+    }
     char* commit(Workspace& workspace, cudaStream_t stream) {
         char* device = static_cast<char*>(workspace.raw(std::max<size_t>(size_, 16)));
         check_cuda(cudaMemcpyAsync(device, pinned_, size_, cudaMemcpyHostToDevice, stream),
@@ -440,20 +451,24 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     char* pinned_read = pinned + prepare_bytes + plan_bytes;
 
     // ---- prepare: wraps, wrapped positions, per-structure extents ---------
-    std::vector<PrepareStructure<T>> prepare(static_cast<size_t>(batch));
-    for (int64_t b = 0; b < batch; ++b) {
-        PrepareStructure<T>& st = prepare[b];
-        st.atom_begin = batch_ptr[b];
-        st.atom_end = batch_ptr[b + 1];
-        for (int k = 0; k < 9; ++k) {
-            st.cell[k] = cell_t[9 * b + k];
-            st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
-        }
-    }
-    std::vector<Reduction<T>> reductions(static_cast<size_t>(batch), neutral_reduction<T>());
+    // Written straight into the pinned upload block by the host pool.
     Upload first(pinned_prepare, prepare_bytes);
-    const size_t off_prepare = first.add(prepare.data(), prepare.size());
-    const size_t off_reduction = first.add(reductions.data(), reductions.size());
+    size_t off_prepare = 0, off_reduction = 0;
+    PrepareStructure<T>* prepare = first.place<PrepareStructure<T>>(static_cast<size_t>(batch), off_prepare);
+    Reduction<T>* neutral = first.place<Reduction<T>>(static_cast<size_t>(batch), off_reduction);
+    const Reduction<T> neutral_value = neutral_reduction<T>();
+    HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
+        for (int64_t b = begin; b < end; ++b) {
+            PrepareStructure<T>& st = prepare[b];
+            st.atom_begin = batch_ptr[b];
+            st.atom_end = batch_ptr[b + 1];
+            for (int k = 0; k < 9; ++k) {
+                st.cell[k] = cell_t[9 * b + k];
+                st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
+            }
+            neutral[b] = neutral_value;
+        }
+    });
     char* first_device = first.commit(workspace, stream);
     auto* d_prepare = reinterpret_cast<PrepareStructure<T>*>(first_device + off_prepare);
     auto* d_reductions = reinterpret_cast<Reduction<T>*>(first_device + off_reduction);
@@ -503,7 +518,10 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                        "a per-source pair count exceeds the int32 range");
     };
 
-    std::vector<StructurePlan<T>> plans(static_cast<size_t>(batch));
+    // Plans are built in place in the pinned upload block.
+    Upload second(pinned_plan, plan_bytes);
+    size_t off_plans = 0;
+    StructurePlan<T>* plans = second.place<StructurePlan<T>>(static_cast<size_t>(batch), off_plans);
     for (int64_t b = 0; b < batch; ++b) {
         StructurePlan<T>& plan = plans[b];
         std::memset(&plan, 0, sizeof(plan));
@@ -520,14 +538,15 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
 
     int64_t total_bins = 0;
     if (any_cell) {
-        check_cuda(cudaMemcpyAsync(pinned_read, d_reductions, reductions.size() * sizeof(Reduction<T>),
+        const size_t reduction_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>);
+        check_cuda(cudaMemcpyAsync(pinned_read, d_reductions, reduction_bytes,
                                    cudaMemcpyDeviceToHost, stream), "read extents");
-        check_cuda(cudaMemcpyAsync(pinned_read + reductions.size() * sizeof(Reduction<T>), d_status,
+        check_cuda(cudaMemcpyAsync(pinned_read + reduction_bytes, d_status,
                                    sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "read status");
         check_cuda(cudaStreamSynchronize(stream), "extents");
-        std::memcpy(reductions.data(), pinned_read, reductions.size() * sizeof(Reduction<T>));
+        const Reduction<T>* reductions = reinterpret_cast<const Reduction<T>*>(pinned_read);
         uint32_t status = 0;
-        std::memcpy(&status, pinned_read + reductions.size() * sizeof(Reduction<T>), sizeof(status));
+        std::memcpy(&status, pinned_read + reduction_bytes, sizeof(status));
         timer.host(3);  // extents read back
         check_status(status);
         std::vector<CellPlan> outcomes(static_cast<size_t>(batch), CellPlan::kUnsafe);
@@ -573,8 +592,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     std::vector<int64_t> cell_bin_prefix;
     for (int32_t b : cell_structs) cell_bin_prefix.push_back(plans[b].bin_begin);
     cell_bin_prefix.push_back(total_bins);
-    Upload second(pinned_plan, plan_bytes);
-    const size_t off_plans = second.add(plans.data(), plans.size());
     const size_t off_cell_prefix = second.add(cell_prefix.data(), cell_prefix.size());
     const size_t off_cell_structs = second.add(cell_structs.data(), cell_structs.size());
     const size_t off_brute_prefix = second.add(brute_prefix.data(), brute_prefix.size());

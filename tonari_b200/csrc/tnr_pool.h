@@ -1,12 +1,17 @@
 // A persistent pool of host threads for the per-structure host work of a
 // call (periodic geometry, cell plans).  Threads are started once per process
 // and sleep between calls; parallel_for hands out fixed-size chunks through
-// an atomic counter and the calling thread takes chunks too.  Calls from
-// several host threads are serialised.
+// an atomic counter and the calling thread takes chunks too.  The caller
+// returns as soon as every chunk is done: a worker that wakes late finds no
+// chunk left and goes back to sleep, so a call never waits for a thread to be
+// scheduled.  Workers poll briefly before sleeping, because the parallel
+// loops of one neighbor-list call follow each other within a millisecond.
+// Calls from several host threads are serialised.
 #pragma once
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdint>
 #include <functional>
@@ -41,14 +46,15 @@ public:
             n_ = n;
             grain_ = grain;
             next_.store(0, std::memory_order_relaxed);
-            active_ = static_cast<int>(std::min<int64_t>(chunks - 1, static_cast<int64_t>(workers_.size())));
-            pending_ = active_;
-            ++generation_;
+            remaining_.store(chunks, std::memory_order_relaxed);
+            generation_.fetch_add(1, std::memory_order_release);
         }
         wake_.notify_all();
         run_chunks(body, n, grain);
         std::unique_lock<std::mutex> lock(mutex_);
-        done_.wait(lock, [&] { return pending_ == 0; });
+        done_.wait(lock, [&] {
+            return remaining_.load(std::memory_order_acquire) == 0 && in_flight_ == 0;
+        });
         body_ = nullptr;
     }
 
@@ -60,7 +66,7 @@ private:
         const unsigned hardware = std::max(1u, std::thread::hardware_concurrency());
         const unsigned count = std::min(hardware, 64u) - 1;
         for (unsigned k = 0; k < count; ++k) {
-            workers_.emplace_back([this, k] { loop(static_cast<int>(k)); });
+            workers_.emplace_back([this] { loop(); });
             workers_.back().detach();
         }
     }
@@ -71,27 +77,39 @@ private:
             const int64_t begin = next_.fetch_add(grain, std::memory_order_relaxed);
             if (begin >= n) return;
             body(begin, std::min(n, begin + grain));
+            if (remaining_.fetch_sub(1, std::memory_order_acq_rel) == 1) {
+                std::lock_guard<std::mutex> lock(mutex_);
+                done_.notify_all();
+            }
         }
     }
 
-    void loop(int index) {
-        uint64_t seen = 0;
+    void loop() {
+        uint64_t seen = generation_.load(std::memory_order_acquire);
         for (;;) {
+            // Poll for up to 200 us, then sleep until the next generation.
+            const auto poll_until = std::chrono::steady_clock::now() + std::chrono::microseconds(200);
+            while (generation_.load(std::memory_order_acquire) == seen &&
+                   std::chrono::steady_clock::now() < poll_until) {
+                std::this_thread::yield();
+            }
             const std::function<void(int64_t, int64_t)>* body;
             int64_t n, grain;
             {
                 std::unique_lock<std::mutex> lock(mutex_);
-                wake_.wait(lock, [&] { return generation_ != seen; });
-                seen = generation_;
-                if (index >= active_) continue;
+                wake_.wait(lock, [&] { return generation_.load(std::memory_order_relaxed) != seen; });
+                seen = generation_.load(std::memory_order_relaxed);
+                if (body_ == nullptr || remaining_.load(std::memory_order_relaxed) == 0) continue;
                 body = body_;
                 n = n_;
                 grain = grain_;
+                ++in_flight_;
             }
             run_chunks(*body, n, grain);
             {
                 std::lock_guard<std::mutex> lock(mutex_);
-                if (--pending_ == 0) done_.notify_one();
+                --in_flight_;
+                done_.notify_all();
             }
         }
     }
@@ -105,9 +123,9 @@ private:
     int64_t n_ = 0;
     int64_t grain_ = 1;
     std::atomic<int64_t> next_{0};
-    int active_ = 0;
-    int pending_ = 0;
-    uint64_t generation_ = 0;
+    std::atomic<int64_t> remaining_{0};
+    int in_flight_ = 0;
+    std::atomic<uint64_t> generation_{0};
 };
 
 }  // namespace tnr
