@@ -1009,9 +1009,13 @@ constexpr int kEmitQueue = 32 * kEmitPerLane;
 template <typename T>
 struct EmitShared {
     StencilRows rows[32];
-    vec4_t<T> pos[32];  // original source position
-    int4 wrap[32];      // source wraps; .w = source atom
-    __align__(32) T cell[32][12];  // source's cell rows, padded for vector loads
+    // Per-source values as separate 4/8-byte arrays: lanes reading different
+    // sources hit different banks.
+    T pos[3][32];        // original source position
+    int32_t wrap[3][32]; // source wraps
+    int32_t atom[32];    // source atom
+    T cell[9][32];       // source's cell (read only when the group's sources
+                         // span several structures)
     int2 mailbox[32];
     int2 queue[2][kEmitQueue];  // (ghost slot, source lane), double buffered
 };
@@ -1071,18 +1075,26 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
             words = (prefix + 31) >> 5;
             mask = args.mask_words + args.bin_word_start[bin] + (k - first);
             mask_stride = n_bin_sources;
-            V ps;
-            ps.x = args.positions[3 * source];
-            ps.y = args.positions[3 * source + 1];
-            ps.z = args.positions[3 * source + 2];
-            ps.w = T(0);
-            sh.pos[lane] = ps;
-            sh.wrap[lane] = make_int4(args.wraps[3 * source], args.wraps[3 * source + 1],
-                                      args.wraps[3 * source + 2], source);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                sh.pos[c][lane] = args.positions[3 * source + c];
+                sh.wrap[c][lane] = args.wraps[3 * source + c];
+            }
+            sh.atom[lane] = source;
             if (need_vector) {
 #pragma unroll
-                for (int c = 0; c < 9; ++c) sh.cell[lane][c] = plan.cell[c];
+                for (int c = 0; c < 9; ++c) sh.cell[c][lane] = plan.cell[c];
             }
+        }
+        // Usually all 32 sources belong to one structure: its cell then
+        // lives in registers instead of being read per pair.
+        const int32_t my_struct = valid ? args.bin_struct[args.source_bin[k]] : -1;
+        const int32_t first_struct = __shfl_sync(kFullMask, my_struct, 0);
+        const bool uniform_cell = __all_sync(kFullMask, !valid || my_struct == first_struct);
+        T group_cell[9];
+        if (need_vector && uniform_cell) {
+#pragma unroll
+            for (int c = 0; c < 9; ++c) group_cell[c] = args.plans[first_struct].cell[c];
         }
         const int32_t batches = static_cast<int32_t>(__reduce_max_sync(kFullMask, static_cast<unsigned>(words)));
         __syncwarp();
@@ -1174,21 +1186,22 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
                 if (e < queued) {
                 const int64_t o = out_row + e;
                 const int32_t r = source_r[m];
-                const int4 ws = sh.wrap[r];
                 int32_t shift[3] = {0, 0, 0};
                 T vec[3] = {T(0), T(0), T(0)};
                 if (need_shift) {
                     // Cell-list shifts fit int32 by construction of the plan.
-                    shift[0] = meta[m].x + ws.x;
-                    shift[1] = meta[m].y + ws.y;
-                    shift[2] = meta[m].z + ws.z;
+                    shift[0] = meta[m].x + sh.wrap[0][r];
+                    shift[1] = meta[m].y + sh.wrap[1][r];
+                    shift[2] = meta[m].z + sh.wrap[2][r];
                 }
                 if (need_vector) {
-                    const V ps = sh.pos[r];
-                    const V c0 = reinterpret_cast<const V*>(sh.cell[r])[0];
-                    const V c1 = reinterpret_cast<const V*>(sh.cell[r])[1];
-                    const V c2 = reinterpret_cast<const V*>(sh.cell[r])[2];
-                    const T cell[9] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w, c2.x};
+                    V ps;
+                    ps.x = sh.pos[0][r];
+                    ps.y = sh.pos[1][r];
+                    ps.z = sh.pos[2][r];
+                    T cell[9];
+#pragma unroll
+                    for (int c = 0; c < 9; ++c) cell[c] = uniform_cell ? group_cell[c] : sh.cell[c][r];
                     const T s0 = static_cast<T>(shift[0]);
                     const T s1 = static_cast<T>(shift[1]);
                     const T s2 = static_cast<T>(shift[2]);
@@ -1199,7 +1212,7 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
                     vec[2] = add_rn(add_rn(add_rn(sub_rn(pt[m].z, ps.z), mul_rn(s0, cell[2])),
                                            mul_rn(s1, cell[5])), mul_rn(s2, cell[8]));
                 }
-                const int64_t s = static_cast<int64_t>(ws.w) + args.index_offset;
+                const int64_t s = static_cast<int64_t>(sh.atom[r]) + args.index_offset;
                 const int64_t t = static_cast<int64_t>(meta[m].w) + args.index_offset;
                 if (wants<Q>(args.out_i, kQ_I)) args.out_i[o] = s;
                 if (wants<Q>(args.out_j, kQ_J)) args.out_j[o] = t;
