@@ -281,7 +281,7 @@ def roofline(w, n_pairs, write_ms, step_ms):
     achieved = traffic_bytes / (write_ms * 1e-3) / 1e9
     per_pair = measured_traffic_per_pair() if w.name.startswith("cfg5") else None
     traffic = int(per_pair * n_pairs) if per_pair else None
-    traffic_source = ("ncu dram read+write of cell_write_kernel on cfg5[:1024], scaled by pairs "
+    traffic_source = ("ncu dram read+write of cell_emit_kernel on cfg5[:1024], scaled by pairs "
                       "(profiles/traffic_cfg5_1024.md)" if traffic else None)
     call = traffic_bytes / (step_ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
