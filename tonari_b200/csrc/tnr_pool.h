@@ -14,6 +14,7 @@
 #include <chrono>
 #include <condition_variable>
 #include <cstdint>
+#include <cstdlib>
 #include <functional>
 #include <mutex>
 #include <thread>
@@ -62,8 +63,15 @@ public:
     HostPool& operator=(const HostPool&) = delete;
 
 private:
+    // One process per GPU shares the host: under a launcher that sets
+    // LOCAL_WORLD_SIZE (torchrun does) each process takes its share of the
+    // cores, so the ranks' pools do not oversubscribe the host.
     HostPool() {
-        const unsigned hardware = std::max(1u, std::thread::hardware_concurrency());
+        unsigned hardware = std::max(1u, std::thread::hardware_concurrency());
+        if (const char* local = std::getenv("LOCAL_WORLD_SIZE")) {
+            const long ranks = std::strtol(local, nullptr, 10);
+            if (ranks > 1) hardware = std::max(1u, hardware / static_cast<unsigned>(ranks));
+        }
         const unsigned count = std::min(hardware, 64u) - 1;
         for (unsigned k = 0; k < count; ++k) {
             workers_.emplace_back([this] { loop(); });
