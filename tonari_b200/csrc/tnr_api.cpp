@@ -387,9 +387,26 @@ CellPlan plan_cell(StructurePlan<T>& plan, const Reduction<T>& reduction, const 
     return CellPlan::kReady;
 }
 
+// Raised when the device's speculative geometry cannot be used; the call is
+// then repeated with the host's exact geometry.
+struct SpeculationFailed {};
+
+// Batches of at least this many float32 structures compute their periodic
+// geometry on the device first and verify it on the host while the search
+// runs (the host's long-double geometry takes about 1 us per structure).
+constexpr int64_t kSpeculativeGeometryBatch = 64;
+
+template <typename T>
+bool speculate_geometry(const tnr_request& request) {
+    if (!std::is_same<T, float>::value) return false;
+    if (request.n_structures < kSpeculativeGeometryBatch || request.n_atoms == 0) return false;
+    const char* flag = std::getenv("TONARI_B200_HOST_GEOMETRY");
+    return !(flag && flag[0] == '1');
+}
+
 template <typename T>
 void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
-         tnr_result& result) {
+         tnr_result& result, bool speculate) {
     using V4 = typename std::conditional<std::is_same<T, float>::value, float4, double4>::type;
     const int64_t n_atoms = request.n_atoms;
     const int64_t batch = request.n_structures;
@@ -429,9 +446,11 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     for (uint8_t& flag : pbc) flag = flag ? 1 : 0;
     std::vector<double> cell64(cell_t.begin(), cell_t.end());
-    const PeriodicGeometry geometry =
-        build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
-    timer.host(1);  // periodic geometry
+    PeriodicGeometry geometry;
+    if (!speculate) {
+        geometry = build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
+    }
+    timer.host(1);  // periodic geometry (host path)
 
     result.n_pairs = 0;
     if (n_atoms == 0) return;
@@ -444,7 +463,8 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     const size_t plan_bytes = static_cast<size_t>(batch) *
         (sizeof(StructurePlan<T>) + 3 * sizeof(int64_t) + 2 * sizeof(int32_t)) +
         8192;
-    const size_t read_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>) + 1024;
+    const size_t read_bytes =
+        static_cast<size_t>(batch) * (sizeof(Reduction<T>) + sizeof(DeviceGeometry)) + 2048;
     char* pinned = g_pinned.reserve(prepare_bytes + plan_bytes + read_bytes);
     char* pinned_prepare = pinned;
     char* pinned_plan = pinned + prepare_bytes;
@@ -459,6 +479,8 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     const Reduction<T> neutral_value = neutral_reduction<T>();
     HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
         for (int64_t b = begin; b < end; ++b) {
+            neutral[b] = neutral_value;
+            if (speculate) continue;  // the geometry kernel writes the prepare records
             PrepareStructure<T>& st = prepare[b];
             st.atom_begin = batch_ptr[b];
             st.atom_end = batch_ptr[b + 1];
@@ -466,7 +488,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                 st.cell[k] = cell_t[9 * b + k];
                 st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
             }
-            neutral[b] = neutral_value;
         }
     });
     char* first_device = first.commit(workspace, stream);
@@ -482,6 +503,13 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     auto* d_wrapped = workspace.get<V4>(n_atoms);
     auto* d_status = workspace.get<uint32_t>(4);
     check_cuda(cudaMemsetAsync(d_status, 0, 4 * sizeof(uint32_t), stream), "memset status");
+    DeviceGeometry* d_geometry = nullptr;
+    if (speculate) {
+        d_geometry = workspace.get<DeviceGeometry>(batch);
+        launch_geometry<T>(static_cast<const T*>(request.cell), request.pbc, d_batch_ptr, batch,
+                           request.cutoff, d_prepare, d_geometry, d_status + 1, stream);
+        check_launch("geometry kernel");
+    }
 
     PrepareArgs<T> prepare_args{static_cast<const T*>(request.positions), n_atoms, d_batch_ptr,
                                 batch, d_prepare, d_atom_struct, d_wraps, d_wrapped,
@@ -490,22 +518,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     check_launch("prepare kernel");
     timer.host(2);  // prepare launched
     timer.mark(1);
-
-    // ---- per-structure algorithm ----------------------------------------
-    std::vector<int32_t> mode(static_cast<size_t>(batch), kModeEmpty);
-    bool any_cell = false;
-    for (int64_t b = 0; b < batch; ++b) {
-        if (counts[b] == 0) continue;
-        const int64_t images = geometry.image_begin[b + 1] - geometry.image_begin[b];
-        bool cell = false;
-        if (request.algorithm == TNR_CELL_LIST) {
-            cell = true;
-        } else if (request.algorithm == TNR_AUTO) {
-            cell = counts[b] > brute_candidates_per_source() / std::max<int64_t>(images, 1);
-        }
-        mode[b] = cell ? kModeCell : kModeBrute;
-        any_cell = any_cell || cell;
-    }
 
     auto check_status = [&](uint32_t status) {
         require_search(!(status & kStatusNonFinite), "positions must contain only finite values");
@@ -518,11 +530,66 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                        "a per-source pair count exceeds the int32 range");
     };
 
-    // Plans are built in place in the pinned upload block.
+    // Speculative geometry: read back the device's geometry with the extents
+    // (one synchronisation) and use it for the plans.  Any flagged structure,
+    // an error status or an image total beyond the limit sends the call to
+    // the exact host path, which decides results and errors.
+    const size_t reduction_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>);
+    const Reduction<T>* reductions = nullptr;
+    if (speculate) {
+        // Pinned read-back block: extents, two status words, then geometry.
+        const size_t geometry_offset = (reduction_bytes + 2 * sizeof(uint32_t) + 255) / 256 * 256;
+        const DeviceGeometry* device_geometry =
+            reinterpret_cast<const DeviceGeometry*>(pinned_read + geometry_offset);
+        check_cuda(cudaMemcpyAsync(pinned_read, d_reductions, reduction_bytes,
+                                   cudaMemcpyDeviceToHost, stream), "read extents");
+        check_cuda(cudaMemcpyAsync(pinned_read + reduction_bytes, d_status, 2 * sizeof(uint32_t),
+                                   cudaMemcpyDeviceToHost, stream), "read status");
+        check_cuda(cudaMemcpyAsync(pinned_read + geometry_offset, d_geometry,
+                                   static_cast<size_t>(batch) * sizeof(DeviceGeometry),
+                                   cudaMemcpyDeviceToHost, stream), "read geometry");
+        check_cuda(cudaStreamSynchronize(stream), "extents");
+        reductions = reinterpret_cast<const Reduction<T>*>(pinned_read);
+        uint32_t status[2] = {0, 0};
+        std::memcpy(status, pinned_read + reduction_bytes, sizeof(status));
+        timer.host(3);  // extents and geometry read back
+        if (status[0] != 0 || status[1] != 0) throw SpeculationFailed{};
+        geometry.duals.resize(static_cast<size_t>(9 * batch));
+        geometry.repeats.resize(static_cast<size_t>(3 * batch));
+        geometry.image_begin.assign(static_cast<size_t>(batch + 1), 0);
+        HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
+            for (int64_t b = begin; b < end; ++b) {
+                const DeviceGeometry& g = device_geometry[b];
+                for (int k = 0; k < 9; ++k) geometry.duals[9 * b + k] = g.dual[k];
+                for (int a = 0; a < 3; ++a) geometry.repeats[3 * b + a] = g.repeats[a];
+            }
+        });
+        for (int64_t b = 0; b < batch; ++b) {
+            geometry.image_begin[b + 1] = geometry.image_begin[b] + device_geometry[b].images;
+            if (geometry.image_begin[b + 1] > (int64_t{1} << 24)) throw SpeculationFailed{};
+        }
+    }
+
+    // ---- per-structure algorithm and plans ---------------------------------
+    // Plans are built in place in the pinned upload block by the host pool;
+    // without speculation this overlaps the prepare kernel, and the cell
+    // plans, which need the extents, follow the read-back.
+    std::vector<int32_t> mode(static_cast<size_t>(batch), kModeEmpty);
+    std::vector<CellPlan> outcomes(static_cast<size_t>(batch), CellPlan::kUnsafe);
     Upload second(pinned_plan, plan_bytes);
     size_t off_plans = 0;
     StructurePlan<T>* plans = second.place<StructurePlan<T>>(static_cast<size_t>(batch), off_plans);
-    for (int64_t b = 0; b < batch; ++b) {
+    auto build_plan = [&](int64_t b) {
+        if (counts[b] != 0) {
+            const int64_t images = geometry.image_begin[b + 1] - geometry.image_begin[b];
+            bool cell = false;
+            if (request.algorithm == TNR_CELL_LIST) {
+                cell = true;
+            } else if (request.algorithm == TNR_AUTO) {
+                cell = counts[b] > brute_candidates_per_source() / std::max<int64_t>(images, 1);
+            }
+            mode[b] = cell ? kModeCell : kModeBrute;
+        }
         StructurePlan<T>& plan = plans[b];
         std::memset(&plan, 0, sizeof(plan));
         plan.atom_begin = batch_ptr[b];
@@ -534,29 +601,38 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         for (int k = 0; k < 9; ++k) plan.cell[k] = cell_t[9 * b + k];
         plan.cutoff_squared = static_cast<T>(request.cutoff * request.cutoff);
         plan.dims[0] = plan.dims[1] = plan.dims[2] = 1;
-    }
+    };
+    auto plan_cells = [&](int64_t b) {
+        if (mode[b] == kModeCell) {
+            outcomes[b] = plan_cell(plans[b], reductions[b], cell_t.data() + 9 * b,
+                                    geometry.duals.data() + 9 * b, request.cutoff);
+        }
+    };
+    HostPool::instance().parallel_for(batch, 256, [&](int64_t begin, int64_t end) {
+        for (int64_t b = begin; b < end; ++b) {
+            build_plan(b);
+            if (speculate) plan_cells(b);
+        }
+    });
+    const bool any_cell = std::any_of(mode.begin(), mode.end(), [](int32_t m) { return m == kModeCell; });
 
     int64_t total_bins = 0;
     if (any_cell) {
-        const size_t reduction_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>);
-        check_cuda(cudaMemcpyAsync(pinned_read, d_reductions, reduction_bytes,
-                                   cudaMemcpyDeviceToHost, stream), "read extents");
-        check_cuda(cudaMemcpyAsync(pinned_read + reduction_bytes, d_status,
-                                   sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "read status");
-        check_cuda(cudaStreamSynchronize(stream), "extents");
-        const Reduction<T>* reductions = reinterpret_cast<const Reduction<T>*>(pinned_read);
-        uint32_t status = 0;
-        std::memcpy(&status, pinned_read + reduction_bytes, sizeof(status));
-        timer.host(3);  // extents read back
-        check_status(status);
-        std::vector<CellPlan> outcomes(static_cast<size_t>(batch), CellPlan::kUnsafe);
-        HostPool::instance().parallel_for(batch, 256, [&](int64_t begin, int64_t end) {
-            for (int64_t b = begin; b < end; ++b) {
-                if (mode[b] != kModeCell) continue;
-                outcomes[b] = plan_cell(plans[b], reductions[b], cell_t.data() + 9 * b,
-                                        geometry.duals.data() + 9 * b, request.cutoff);
-            }
-        });
+        if (!speculate) {
+            check_cuda(cudaMemcpyAsync(pinned_read, d_reductions, reduction_bytes,
+                                       cudaMemcpyDeviceToHost, stream), "read extents");
+            check_cuda(cudaMemcpyAsync(pinned_read + reduction_bytes, d_status,
+                                       sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "read status");
+            check_cuda(cudaStreamSynchronize(stream), "extents");
+            reductions = reinterpret_cast<const Reduction<T>*>(pinned_read);
+            uint32_t status = 0;
+            std::memcpy(&status, pinned_read + reduction_bytes, sizeof(status));
+            timer.host(3);  // extents read back
+            check_status(status);
+            HostPool::instance().parallel_for(batch, 256, [&](int64_t begin, int64_t end) {
+                for (int64_t b = begin; b < end; ++b) plan_cells(b);
+            });
+        }
         for (int64_t b = 0; b < batch; ++b) {
             if (mode[b] != kModeCell) continue;
             StructurePlan<T>& plan = plans[b];
@@ -745,18 +821,45 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     timer.mark(3);
     timer.host(6);  // count pass launched
+    if (speculate) {
+        // While the search runs: the exact geometry (the reference's long-
+        // double arithmetic) must give the same T duals and image ranges as
+        // the device, else the call is repeated on the host path.  Its input
+        // errors are raised by that repeat, in the reference's order.
+        const PeriodicGeometry exact =
+            build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
+        for (int64_t b = 0; b < batch; ++b) {
+            for (int a = 0; a < 3; ++a) {
+                if (exact.repeats[3 * b + a] != geometry.repeats[3 * b + a]) throw SpeculationFailed{};
+            }
+            if (exact.image_begin[b + 1] != geometry.image_begin[b + 1]) throw SpeculationFailed{};
+        }
+        // The duals may differ in their last bits (the device rounds in
+        // double); what the search used of them is the wraps, which the
+        // device now recomputes with the exact duals (status word 2).
+        T* exact_duals = reinterpret_cast<T*>(pinned_prepare);
+        for (int64_t k = 0; k < 9 * batch; ++k) exact_duals[k] = static_cast<T>(exact.duals[k]);
+        T* d_exact_duals = workspace.get<T>(9 * batch);
+        check_cuda(cudaMemcpyAsync(d_exact_duals, exact_duals, 9 * batch * sizeof(T),
+                                   cudaMemcpyHostToDevice, stream), "upload exact duals");
+        launch_verify_wraps<T>(static_cast<const T*>(request.positions), n_atoms, d_atom_struct,
+                               d_exact_duals, d_wraps, d_status + 2, stream);
+        check_launch("wrap check kernel");
+    }
     launch_scan_counts(d_counts, n_atoms, d_pair_start, d_scan_workspace, d_status, stream);
     check_launch("pair scan kernel");
     timer.mark(4);
     check_cuda(cudaMemcpyAsync(pinned_read, d_pair_start + n_atoms, sizeof(int64_t),
                                cudaMemcpyDeviceToHost, stream), "read pair total");
-    check_cuda(cudaMemcpyAsync(pinned_read + sizeof(int64_t), d_status, sizeof(uint32_t),
+    check_cuda(cudaMemcpyAsync(pinned_read + sizeof(int64_t), d_status, 3 * sizeof(uint32_t),
                                cudaMemcpyDeviceToHost, stream), "read status");
     check_cuda(cudaStreamSynchronize(stream), "pair total");
     int64_t n_pairs = 0;
-    uint32_t status = 0;
+    uint32_t status = 0, wraps_differ = 0;
     std::memcpy(&n_pairs, pinned_read, sizeof(n_pairs));
     std::memcpy(&status, pinned_read + sizeof(int64_t), sizeof(status));
+    std::memcpy(&wraps_differ, pinned_read + sizeof(int64_t) + 2 * sizeof(uint32_t), sizeof(wraps_differ));
+    if (speculate && wraps_differ) throw SpeculationFailed{};
     timer.host(7);  // pair total read back
     check_status(status);
     require_search(n_pairs >= 0, "neighbor-list output exceeds the int64 range");
@@ -792,6 +895,27 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     timer.mark(6);
     timer.host(8);  // write pass launched
     timer.finish();
+}
+
+// Runs the call, speculating on the device geometry where that pays off.  A
+// failed speculation (or any input or search error raised under it) repeats
+// the call on the host path, whose results and errors are the reference's.
+template <typename T>
+void run_call(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
+              tnr_result& result) {
+    if (speculate_geometry<T>(request)) {
+        try {
+            run<T>(request, workspace, stream, result, true);
+            return;
+        } catch (const SpeculationFailed&) {
+        } catch (const InputError&) {
+        } catch (const SearchError&) {
+        }
+        check_cuda(cudaStreamSynchronize(stream), "speculative geometry");
+        workspace.release_outputs();
+        result = tnr_result{};
+    }
+    run<T>(request, workspace, stream, result, false);
 }
 
 void set_message(char* message, size_t length, const char* text) {
@@ -833,9 +957,9 @@ int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator
                       "positions must have dtype float32 or float64");
         tnr_result local{};
         if (request->dtype == TNR_FLOAT32) {
-            run<float>(*request, workspace, stream, local);
+            run_call<float>(*request, workspace, stream, local);
         } else {
-            run<double>(*request, workspace, stream, local);
+            run_call<double>(*request, workspace, stream, local);
         }
         workspace.keep_outputs();
         *result = local;

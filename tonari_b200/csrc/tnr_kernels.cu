@@ -36,6 +36,132 @@ constexpr int kSearchThreads = 256;
 constexpr int kSearchWarps = kSearchThreads / 32;
 
 // ---------------------------------------------------------------------------
+// geometry (speculative, double precision)
+// ---------------------------------------------------------------------------
+
+// The reference's active pseudo-inverse (tonari csrc/core/geometry.cpp:15-118)
+// and image ranges (:123-219) in double: same rotation sequence, convergence
+// test, singular-value tolerance and ceil(cutoff * |dual column|).  The host
+// compares the T-cast duals and the repeats with its long-double result.
+template <typename T>
+__global__ void geometry_kernel(const T* __restrict__ cell, const uint8_t* __restrict__ pbc,
+                                const int64_t* __restrict__ batch_ptr, int64_t batch, double cutoff,
+                                PrepareStructure<T>* __restrict__ prepare,
+                                DeviceGeometry* __restrict__ out, uint32_t* flags) {
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= batch) return;
+    const double eps = 2.220446049250313e-16;  // double epsilon
+    double c[9];
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+        c[k] = static_cast<double>(cell[9 * b + k]);
+        bad = bad || !isfinite(c[k]);
+    }
+    const int64_t atoms = batch_ptr[b + 1] - batch_ptr[b];
+    DeviceGeometry g;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) g.dual[k] = 0.0;
+    g.repeats[0] = g.repeats[1] = g.repeats[2] = 0;
+    g.images = 0;
+    if (!bad && atoms > 0) {
+        int axes[3];
+        int active = 0;
+        for (int a = 0; a < 3; ++a) {
+            if (pbc[3 * b + a] != 0) axes[active++] = a;
+        }
+        if (active > 0) {
+            double columns[3][3] = {};
+            double right[3][3] = {};
+            for (int col = 0; col < active; ++col) {
+                right[col][col] = 1.0;
+                for (int x = 0; x < 3; ++x) columns[x][col] = c[3 * axes[col] + x];
+            }
+            for (int sweep = 0; sweep < 64; ++sweep) {
+                bool converged = true;
+                for (int p = 0; p < active; ++p) {
+                    for (int q = p + 1; q < active; ++q) {
+                        double npp = 0.0, nqq = 0.0, npq = 0.0;
+                        for (int x = 0; x < 3; ++x) {
+                            npp = __dadd_rn(npp, __dmul_rn(columns[x][p], columns[x][p]));
+                            nqq = __dadd_rn(nqq, __dmul_rn(columns[x][q], columns[x][q]));
+                            npq = __dadd_rn(npq, __dmul_rn(columns[x][p], columns[x][q]));
+                        }
+                        if (fabs(npq) <= 8 * eps * sqrt(npp * nqq)) continue;
+                        converged = false;
+                        const double tau = (nqq - npp) / (2 * npq);
+                        const double t = tau == 0.0 ? 1.0 : copysign(1.0, tau) / (fabs(tau) + hypot(1.0, tau));
+                        const double cs = 1.0 / hypot(1.0, t);
+                        const double sn = cs * t;
+                        for (int x = 0; x < 3; ++x) {
+                            const double u = columns[x][p], v = columns[x][q];
+                            columns[x][p] = __dsub_rn(__dmul_rn(cs, u), __dmul_rn(sn, v));
+                            columns[x][q] = __dadd_rn(__dmul_rn(sn, u), __dmul_rn(cs, v));
+                        }
+                        for (int r = 0; r < active; ++r) {
+                            const double u = right[r][p], v = right[r][q];
+                            right[r][p] = __dsub_rn(__dmul_rn(cs, u), __dmul_rn(sn, v));
+                            right[r][q] = __dadd_rn(__dmul_rn(sn, u), __dmul_rn(cs, v));
+                        }
+                    }
+                }
+                if (converged) break;
+            }
+            double sigma[3] = {};
+            double largest = 0.0, smallest = INFINITY;
+            for (int col = 0; col < active; ++col) {
+                double n2 = 0.0;
+                for (int x = 0; x < 3; ++x) n2 = __dadd_rn(n2, __dmul_rn(columns[x][col], columns[x][col]));
+                sigma[col] = sqrt(n2);
+                largest = fmax(largest, sigma[col]);
+                smallest = fmin(smallest, sigma[col]);
+            }
+            // The host tolerance is eps * 3 * max(largest, 1); a margin keeps
+            // borderline cells on the exact host path.
+            if (!(smallest > eps * 3 * fmax(largest, 1.0) * 4)) bad = true;
+            int64_t images = 1;
+            for (int col = 0; col < active && !bad; ++col) {
+                double n2 = 0.0;
+                for (int x = 0; x < 3; ++x) {
+                    double value = 0.0;
+                    for (int s = 0; s < active; ++s) {
+                        value = __dadd_rn(value, __ddiv_rn(__dmul_rn(columns[x][s], right[col][s]),
+                                                           __dmul_rn(sigma[s], sigma[s])));
+                    }
+                    bad = bad || !isfinite(value);
+                    g.dual[3 * x + axes[col]] = value;
+                    n2 = __dadd_rn(n2, __dmul_rn(value, value));
+                }
+                const double repeat = ceil(cutoff * sqrt(n2));
+                if (!(repeat <= 1048576.0)) {
+                    bad = true;
+                } else {
+                    g.repeats[axes[col]] = static_cast<int32_t>(repeat);
+                }
+            }
+            for (int a = 0; a < 3 && !bad; ++a) {
+                images *= 2 * static_cast<int64_t>(g.repeats[a]) + 1;
+                if (images > (int64_t{1} << 24)) bad = true;
+            }
+            g.images = bad ? 0 : static_cast<int32_t>(images);
+        } else {
+            g.images = 1;
+        }
+    }
+    PrepareStructure<T> st;
+    st.atom_begin = batch_ptr[b];
+    st.atom_end = batch_ptr[b + 1];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+        st.cell[k] = cell[9 * b + k];
+        st.dual[k] = static_cast<T>(g.dual[k]);
+    }
+    prepare[b] = st;
+    out[b] = g;
+    if (bad) atomicOr(flags, 1u);
+}
+
+// ---------------------------------------------------------------------------
 // prepare
 // ---------------------------------------------------------------------------
 
@@ -227,6 +353,29 @@ __global__ void __launch_bounds__(kPrepareThreads) prepare_kernel(PrepareArgs<T>
     }
 }
 
+
+// Check of a speculative geometry: the wraps of every atom recomputed with
+// the exact (host, long-double) duals cast to T must equal the wraps the
+// call used; any difference sets *flag and the call is repeated on the host
+// path.  Equal wraps (with equal image ranges, checked on the host) make
+// every later step identical to the host-geometry call.
+template <typename T>
+__global__ void __launch_bounds__(kPrepareThreads) verify_wraps_kernel(
+    const T* __restrict__ positions, int64_t n_atoms, const int32_t* __restrict__ atom_struct,
+    const T* __restrict__ duals, const int32_t* __restrict__ wraps, uint32_t* flag) {
+    const int64_t atom = static_cast<int64_t>(blockIdx.x) * kPrepareThreads + threadIdx.x;
+    if (atom >= n_atoms) return;
+    const T* dual = duals + 9 * static_cast<int64_t>(atom_struct[atom]);
+    const double p0 = positions[3 * atom], p1 = positions[3 * atom + 1], p2 = positions[3 * atom + 2];
+    bool same = true;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+        const DotFloor f = dot_floor(p0, p1, p2, dual[a], dual[3 + a], dual[6 + a]);
+        same = same && isfinite(f.approx) && f.approx >= -2147483648.0 && f.approx < 2147483648.0 &&
+               static_cast<int32_t>(f.floor_value) == wraps[3 * atom + a];
+    }
+    if (!same) atomicOr(flag, 1u);
+}
 
 // ---------------------------------------------------------------------------
 // bin: histogram (pass 1) and scatter (pass 2) of culled image copies
@@ -1458,6 +1607,26 @@ thread_local int64_t g_kernel_launches = 0;
 int64_t launched_kernels() { return g_kernel_launches; }
 
 template <typename T>
+void launch_geometry(const T* cell, const uint8_t* pbc, const int64_t* batch_ptr, int64_t batch,
+                     double cutoff, PrepareStructure<T>* prepare, DeviceGeometry* geometry,
+                     uint32_t* flags, cudaStream_t stream) {
+    if (batch == 0) return;
+    geometry_kernel<T><<<static_cast<unsigned>(blocks_for(batch, 128)), 128, 0, stream>>>(
+        cell, pbc, batch_ptr, batch, cutoff, prepare, geometry, flags);
+    ++g_kernel_launches;
+}
+
+template <typename T>
+void launch_verify_wraps(const T* positions, int64_t n_atoms, const int32_t* atom_struct,
+                         const T* duals, const int32_t* wraps, uint32_t* flag, cudaStream_t stream) {
+    if (n_atoms == 0) return;
+    verify_wraps_kernel<T><<<static_cast<unsigned>(blocks_for(n_atoms, kPrepareThreads)),
+                             kPrepareThreads, 0, stream>>>(positions, n_atoms, atom_struct, duals,
+                                                           wraps, flag);
+    ++g_kernel_launches;
+}
+
+template <typename T>
 void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream) {
     if (args.n_atoms == 0) return;
     prepare_kernel<T><<<static_cast<unsigned>(blocks_for(args.n_atoms, kPrepareThreads)),
@@ -1598,6 +1767,11 @@ void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* works
 
 #define TNR_INSTANTIATE(T)                                                                 \
     template void launch_prepare<T>(const PrepareArgs<T>&, cudaStream_t);                  \
+    template void launch_verify_wraps<T>(const T*, int64_t, const int32_t*, const T*,         \
+                                         const int32_t*, uint32_t*, cudaStream_t);            \
+    template void launch_geometry<T>(const T*, const uint8_t*, const int64_t*, int64_t, double, \
+                                     PrepareStructure<T>*, DeviceGeometry*, uint32_t*,         \
+                                     cudaStream_t);                                            \
     template void launch_bin<T>(const BinArgs<T>&, bool, cudaStream_t);                     \
     template void launch_image_table<T>(const StructurePlan<T>*, int64_t, int4*, void*,    \
                                         cudaStream_t);                                       \

@@ -89,6 +89,32 @@ struct SearchArgs {
     int32_t include_self;
 };
 
+// Speculative periodic geometry on the device (one thread per structure):
+// the reference's one-sided Jacobi pseudo-inverse evaluated in double instead
+// of long double.  Writes the prepare records (cell, dual cast to T), the
+// double duals, repeats and image counts; sets `flags` to nonzero when any
+// structure needs the host's exact treatment (non-finite cell, near-singular
+// active rows, out-of-range duals or repeats, more than 2^24 images).  The
+// host checks the image ranges against its long-double geometry, and the
+// device checks every atom's wraps against the exact duals
+// (launch_verify_wraps), before the call's output is trusted.
+struct DeviceGeometry {
+    double dual[9];      // [cartesian][axis]
+    int32_t repeats[3];
+    int32_t images;      // 0 for an empty structure
+};
+
+template <typename T>
+void launch_geometry(const T* cell, const uint8_t* pbc, const int64_t* batch_ptr, int64_t batch,
+                     double cutoff, PrepareStructure<T>* prepare, DeviceGeometry* geometry,
+                     uint32_t* flags, cudaStream_t stream);
+
+// Sets *flag when any atom's wraps, recomputed with `duals` ([B][9] in T,
+// [cartesian][axis]), differ from `wraps`.
+template <typename T>
+void launch_verify_wraps(const T* positions, int64_t n_atoms, const int32_t* atom_struct,
+                         const T* duals, const int32_t* wraps, uint32_t* flag, cudaStream_t stream);
+
 template <typename T>
 void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream);
 
