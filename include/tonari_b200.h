@@ -51,7 +51,12 @@ enum tnr_quantity {
     TNR_Q_P = 1u << 2, /* (E,2) int64 [source, target]  */
     TNR_Q_S = 1u << 3, /* (E,3) int32 cell shift        */
     TNR_Q_d = 1u << 4, /* (E,)  T     distance          */
-    TNR_Q_D = 1u << 5  /* (E,3) T     displacement      */
+    TNR_Q_D = 1u << 5, /* (E,3) T     displacement      */
+    /* (2,E) int64 graph layout: row 0 sources, row 1 targets, one buffer.
+     * No counterpart in the reference's core API, whose adapters transpose P
+     * (tonari docs/design.md:61, README.md:97); it cannot be combined with
+     * TNR_Q_I or TNR_Q_J and is not offered by tnr_neighbor_list_static. */
+    TNR_Q_EDGE = 1u << 6
 };
 
 /* Device allocation callback.  Must return device memory aligned to at least
@@ -96,6 +101,7 @@ typedef struct {
     int32_t* S;      /* NULL unless TNR_Q_S */
     void* d;         /* NULL unless TNR_Q_d */
     void* D;         /* NULL unless TNR_Q_D */
+    int64_t* edge_index; /* NULL unless TNR_Q_EDGE: (2,E) */
 } tnr_result;
 
 /*

@@ -35,7 +35,8 @@ def test_version_and_struct_layout():
     assert _cabi.Request.cutoff.offset == 80
     assert _cabi.Request.index_offset.offset == 104
     assert ctypes.sizeof(_cabi.Request) == 120
-    assert ctypes.sizeof(_cabi.Result) == 56
+    assert _cabi.Result.edge_index.offset == 56
+    assert ctypes.sizeof(_cabi.Result) == 64
 
 
 def test_input_errors_are_reported_without_device_work():

@@ -1,5 +1,6 @@
 """tonari_b200 -- B200-native (sm_100a) CUDA provider of tonari's neighbor list."""
 from .api import neighbor_list
+from .graph import neighbor_graph
 
 __version__ = "0.1.0"
-__all__ = ["neighbor_list"]
+__all__ = ["neighbor_list", "neighbor_graph"]

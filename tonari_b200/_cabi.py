@@ -28,7 +28,7 @@ class Request(ctypes.Structure):
 
 class Result(ctypes.Structure):
     _fields_ = [("n_pairs", ctypes.c_int64)] + [
-        (name, ctypes.c_void_p) for name in ("i", "j", "P", "S", "d", "D")]
+        (name, ctypes.c_void_p) for name in ("i", "j", "P", "S", "d", "D", "edge_index")]
 
 
 EXPORTED = ("tnr_neighbor_list", "tnr_neighbor_list_static", "tnr_version",

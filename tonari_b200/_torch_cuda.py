@@ -3,14 +3,15 @@
 ``neighbor_list`` has the signature of tonari csrc/torch/bindings_cuda.cpp:59-68
 and returns ``[P (E,2) int64, S (E,3) int32]``.  A reference installation can
 use it by making ``tonari._extensions.load_torch_cuda`` return this module.
-``neighbor_list_fused`` additionally emits i/j/d/D from the same kernel.
+``neighbor_list_fused`` additionally emits i/j/d/D from the same kernel, and
+"E", the (2,E) edge_index graph layout (one buffer, no transpose).
 """
 from __future__ import annotations
 
 import torch
 from torch import Tensor
 
-_INDEX = {"i": 0, "j": 1, "P": 2, "S": 3, "d": 4, "D": 5}
+_INDEX = {"i": 0, "j": 1, "P": 2, "S": 3, "d": 4, "D": 5, "E": 6}
 
 
 def neighbor_list(

@@ -875,8 +875,9 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     if (q & TNR_Q_S) result.S = workspace.output<int32_t>(3 * e);
     if (q & TNR_Q_d) result.d = workspace.output<T>(e);
     if (q & TNR_Q_D) result.D = workspace.output<T>(3 * e);
-    search.out_i = result.i;
-    search.out_j = result.j;
+    if (q & TNR_Q_EDGE) result.edge_index = workspace.output<int64_t>(2 * e);
+    search.out_i = result.edge_index ? result.edge_index : result.i;
+    search.out_j = result.edge_index ? result.edge_index + e : result.j;
     search.out_P = result.P;
     search.out_S = result.S;
     search.out_d = static_cast<T*>(result.d);
@@ -955,6 +956,9 @@ int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator
                       "algorithm must be 'auto', 'brute_force', or 'cell_list'");
         require_input(request->dtype == TNR_FLOAT32 || request->dtype == TNR_FLOAT64,
                       "positions must have dtype float32 or float64");
+        require_input(!(request->quantities & TNR_Q_EDGE) ||
+                          !(request->quantities & (TNR_Q_I | TNR_Q_J)),
+                      "edge_index cannot be combined with i or j");
         tnr_result local{};
         if (request->dtype == TNR_FLOAT32) {
             run_call<float>(*request, workspace, stream, local);

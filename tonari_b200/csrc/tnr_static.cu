@@ -301,6 +301,8 @@ extern "C" int tnr_neighbor_list_static(const tnr_request* request, tnr_stream s
                       "batch_ptr must have shape (B + 1,)");
         require_input(request->dtype == TNR_FLOAT32 || request->dtype == TNR_FLOAT64,
                       "positions must have dtype float32 or float64");
+        require_input(!(request->quantities & TNR_Q_EDGE),
+                      "edge_index is not offered by the allocation-free entry point");
         if (request->dtype == TNR_FLOAT32) {
             run_static<float>(*request, stream, pair_capacity, *result);
         } else {

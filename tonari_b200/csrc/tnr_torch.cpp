@@ -60,6 +60,7 @@ uint32_t parse_quantities(const std::string& quantities) {
             case 'S': mask |= TNR_Q_S; break;
             case 'd': mask |= TNR_Q_d; break;
             case 'D': mask |= TNR_Q_D; break;
+            case 'E': mask |= TNR_Q_EDGE; break;  // (2,E) graph layout
             default: TORCH_CHECK_VALUE(false, "unsupported quantities: '", std::string(1, q), "'");
         }
     }
@@ -148,6 +149,7 @@ std::vector<at::Tensor> neighbor_list_cuda(const at::Tensor& positions, const at
     outputs.push_back(take(context, result.S, at::kInt, {result.S ? e : 0, 3}, options));
     outputs.push_back(take(context, result.d, real, {result.d ? e : 0}, options));
     outputs.push_back(take(context, result.D, real, {result.D ? e : 0, 3}, options));
+    outputs.push_back(take(context, result.edge_index, at::kLong, {2, result.edge_index ? e : 0}, options));
     return outputs;
 }
 
