@@ -138,6 +138,28 @@ int tnr_neighbor_list_static(const tnr_request* request, tnr_stream stream,
                              int64_t pair_capacity, tnr_result* result, char* message,
                              size_t message_length);
 
+/* Candidate pairs for tnr_filter_pairs (device arrays, M rows). */
+typedef struct {
+    const int64_t* pairs;  /* (M,2) int64 [source, target], indices include index_offset */
+    const int32_t* shifts; /* (M,3) int32 cell shifts */
+    int64_t n_candidates;  /* M */
+} tnr_candidates;
+
+/*
+ * No counterpart in the reference, which lists Verlet-skin reuse as future
+ * work (tonari docs/design.md:127).  Keeps the candidate pairs (built by
+ * tnr_neighbor_list with cutoff + skin) whose public displacement at the
+ * current positions, pos[j] - pos[i] + S . cell[b(i)], evaluated exactly as
+ * tnr_neighbor_list's decisive test, is strictly shorter than
+ * request->cutoff; the kept pairs keep their candidate order.  Uses
+ * request->dtype, n_atoms, n_structures, positions, batch_ptr, cell, cutoff,
+ * quantities and index_offset; the other request fields are ignored.
+ * Outputs are allocated like tnr_neighbor_list's.
+ */
+int tnr_filter_pairs(const tnr_request* request, const tnr_candidates* candidates,
+                     const tnr_allocator* allocator, tnr_stream stream, tnr_result* result,
+                     char* message, size_t message_length);
+
 /* Library version string ("major.minor.patch"). */
 const char* tnr_version(void);
 

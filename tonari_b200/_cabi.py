@@ -32,7 +32,8 @@ class Result(ctypes.Structure):
 
 
 EXPORTED = ("tnr_neighbor_list", "tnr_neighbor_list_static", "tnr_version",
-            "tnr_last_launch_count", "tnr_last_phase_times", "tnr_last_host_times")
+            "tnr_last_launch_count", "tnr_last_phase_times", "tnr_last_host_times",
+            "tnr_filter_pairs")
 
 
 @lru_cache

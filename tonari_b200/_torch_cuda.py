@@ -52,3 +52,22 @@ def neighbor_list_fused(
         bool(include_self), algorithm, bool(sorted), wanted, int(index_offset),
     )
     return {q: outputs[_INDEX[q]] for q in wanted}
+
+
+def filter_pairs(
+    positions: Tensor,
+    batch_ptr: Tensor,
+    cell: Tensor,
+    pairs: Tensor,
+    shifts: Tensor,
+    cutoff: float,
+    quantities: str,
+    index_offset: int = 0,
+) -> dict[str, Tensor]:
+    """The candidate pairs whose exact distance at `positions` is below
+    `cutoff`, in candidate order, as ``{quantity: tensor}``."""
+    wanted = "".join(dict.fromkeys(quantities))
+    outputs = torch.ops.tonari_b200.filter_pairs(
+        positions, batch_ptr, cell, pairs, shifts, float(cutoff), wanted, int(index_offset),
+    )
+    return {q: outputs[_INDEX[q]] for q in wanted}

@@ -898,6 +898,62 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     timer.finish();
 }
 
+// Verlet-skin filter: count pass (ballot words, per-block counts), scan of
+// the block counts, exact-size outputs, write pass.
+template <typename T>
+void run_filter(const tnr_request& request, const tnr_candidates& candidates,
+                Workspace& workspace, cudaStream_t stream, tnr_result& result) {
+    const int64_t m = candidates.n_candidates;
+    result.n_pairs = 0;
+    if (m == 0) return;
+    require_input(candidates.pairs != nullptr && candidates.shifts != nullptr,
+                  "candidate pairs and shifts are required");
+    FilterArgs<T> args{};
+    args.positions = static_cast<const T*>(request.positions);
+    args.batch_ptr = request.batch_ptr;
+    args.batch = request.n_structures;
+    args.cell = static_cast<const T*>(request.cell);
+    args.pairs = candidates.pairs;
+    args.shifts = candidates.shifts;
+    args.n_candidates = m;
+    args.index_offset = request.index_offset;
+    args.cutoff_squared = static_cast<T>(request.cutoff * request.cutoff);
+    const int64_t blocks = (m + kFilterThreads - 1) / kFilterThreads;
+    args.keep_words = workspace.get<uint32_t>((m + 31) / 32);
+    args.block_counts = workspace.get<uint32_t>(blocks);
+    auto* block_start = workspace.get<int64_t>(blocks + 1);
+    void* scan_workspace = workspace.raw(scan_workspace_bytes(blocks));
+    launch_filter(args, false, stream);
+    check_launch("filter count kernel");
+    launch_scan_counts(args.block_counts, blocks, block_start, scan_workspace, nullptr, stream);
+    check_launch("filter scan kernel");
+    int64_t* total = reinterpret_cast<int64_t*>(g_pinned.reserve(64));
+    check_cuda(cudaMemcpyAsync(total, block_start + blocks, sizeof(int64_t), cudaMemcpyDeviceToHost,
+                               stream), "read filter total");
+    check_cuda(cudaStreamSynchronize(stream), "filter total");
+    const int64_t n_pairs = *total;
+    result.n_pairs = n_pairs;
+    if (n_pairs == 0) return;
+    const uint32_t q = request.quantities;
+    const size_t e = static_cast<size_t>(n_pairs);
+    if (q & TNR_Q_I) result.i = workspace.output<int64_t>(e);
+    if (q & TNR_Q_J) result.j = workspace.output<int64_t>(e);
+    if (q & TNR_Q_P) result.P = workspace.output<int64_t>(2 * e);
+    if (q & TNR_Q_S) result.S = workspace.output<int32_t>(3 * e);
+    if (q & TNR_Q_d) result.d = workspace.output<T>(e);
+    if (q & TNR_Q_D) result.D = workspace.output<T>(3 * e);
+    if (q & TNR_Q_EDGE) result.edge_index = workspace.output<int64_t>(2 * e);
+    args.block_start = block_start;
+    args.out_i = result.edge_index ? result.edge_index : result.i;
+    args.out_j = result.edge_index ? result.edge_index + e : result.j;
+    args.out_P = result.P;
+    args.out_S = result.S;
+    args.out_d = static_cast<T*>(result.d);
+    args.out_D = static_cast<T*>(result.D);
+    launch_filter(args, true, stream);
+    check_launch("filter write kernel");
+}
+
 // Runs the call, speculating on the device geometry where that pays off.  A
 // failed speculation (or any input or search error raised under it) repeats
 // the call on the host path, whose results and errors are the reference's.
@@ -991,6 +1047,57 @@ int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator
 const char* tnr_version(void) { return "0.1.0"; }
 
 int64_t tnr_last_launch_count(void) { return tnr::g_launches; }
+
+int tnr_filter_pairs(const tnr_request* request, const tnr_candidates* candidates,
+                     const tnr_allocator* allocator, tnr_stream stream_handle, tnr_result* result,
+                     char* message, size_t message_length) {
+    using namespace tnr;
+    if (request == nullptr || candidates == nullptr || result == nullptr) {
+        set_message(message, message_length, "request, candidates and result must not be null");
+        return TNR_INPUT_ERROR;
+    }
+    *result = tnr_result{};
+    g_launches = 0;
+    const int64_t launches_before = launched_kernels();
+    tnr_allocator chosen{nullptr, default_allocate, default_release};
+    if (allocator && allocator->allocate && allocator->release) chosen = *allocator;
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_handle);
+    Workspace workspace(chosen, stream);
+    try {
+        require_input(std::isfinite(request->cutoff) && request->cutoff > 0,
+                      "cutoff must be finite and positive");
+        require_input(request->n_structures >= 1 && request->batch_ptr != nullptr,
+                      "batch_ptr must have shape (B + 1,)");
+        require_input(candidates->n_candidates >= 0, "the candidate count must not be negative");
+        require_input(request->dtype == TNR_FLOAT32 || request->dtype == TNR_FLOAT64,
+                      "positions must have dtype float32 or float64");
+        require_input(!(request->quantities & TNR_Q_EDGE) ||
+                          !(request->quantities & (TNR_Q_I | TNR_Q_J)),
+                      "edge_index cannot be combined with i or j");
+        tnr_result local{};
+        if (request->dtype == TNR_FLOAT32) {
+            run_filter<float>(*request, *candidates, workspace, stream, local);
+        } else {
+            run_filter<double>(*request, *candidates, workspace, stream, local);
+        }
+        workspace.keep_outputs();
+        *result = local;
+        g_launches = launched_kernels() - launches_before;
+        return TNR_OK;
+    } catch (const InputError& error) {
+        workspace.release_outputs();
+        set_message(message, message_length, error.what());
+        return TNR_INPUT_ERROR;
+    } catch (const std::bad_alloc&) {
+        workspace.release_outputs();
+        set_message(message, message_length, "device allocation failed");
+        return TNR_ALLOC_ERROR;
+    } catch (const std::exception& error) {
+        workspace.release_outputs();
+        set_message(message, message_length, error.what());
+        return TNR_CUDA_ERROR;
+    }
+}
 
 int tnr_last_host_times(double* times_ms, int capacity) {
     const int count = std::min(capacity, tnr::kHostMarks);

@@ -1533,6 +1533,84 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
     }
 }
 
+// Candidate filter for Verlet-skin reuse: thread per candidate pair; the
+// decisive test is the one of the search kernels (exact_component in the
+// reference's order, exact_norm2 < (T)(cutoff^2)).  Pass 1 stores one ballot
+// word per warp and one count per block; pass 2 writes the kept pairs at
+// block offset + rank, so they keep their candidate order.
+template <typename T>
+__device__ __forceinline__ bool filter_candidate(const FilterArgs<T>& a, int64_t k, int64_t& source,
+                                                 int64_t& target, long long (&shift)[3], T (&vec)[3]) {
+    source = a.pairs[2 * k] - a.index_offset;
+    target = a.pairs[2 * k + 1] - a.index_offset;
+    shift[0] = a.shifts[3 * k];
+    shift[1] = a.shifts[3 * k + 1];
+    shift[2] = a.shifts[3 * k + 2];
+    const int32_t b = structure_of(a.batch_ptr, a.batch, source);
+    T cell[9];
+#pragma unroll
+    for (int c = 0; c < 9; ++c) cell[c] = a.cell[9 * static_cast<int64_t>(b) + c];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        vec[c] = exact_component(a.positions[3 * target + c], a.positions[3 * source + c], shift, cell, c);
+    }
+    return exact_norm2(vec[0], vec[1], vec[2]) < a.cutoff_squared;
+}
+
+template <typename T, bool Write>
+__global__ void __launch_bounds__(kFilterThreads) filter_kernel(FilterArgs<T> a) {
+    __shared__ uint32_t warp_counts[kFilterThreads / 32];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t k = static_cast<int64_t>(blockIdx.x) * kFilterThreads + threadIdx.x;
+    if constexpr (!Write) {
+        int64_t source = 0, target = 0;
+        long long shift[3];
+        T vec[3];
+        const bool keep = k < a.n_candidates && filter_candidate(a, k, source, target, shift, vec);
+        const uint32_t word = __ballot_sync(kFullMask, keep);
+        if (lane == 0) {
+            if ((k >> 5) < (a.n_candidates + 31) / 32) a.keep_words[k >> 5] = word;
+            warp_counts[warp] = __popc(word);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t total = 0;
+            for (int w = 0; w < kFilterThreads / 32; ++w) total += warp_counts[w];
+            a.block_counts[blockIdx.x] = total;
+        }
+    } else {
+        const int64_t word_index = k >> 5;  // the same for the whole warp
+        const uint32_t word = word_index < (a.n_candidates + 31) / 32 ? a.keep_words[word_index] : 0u;
+        if (lane == 0) warp_counts[warp] = __popc(word);
+        __syncthreads();
+        int64_t row = a.block_start[blockIdx.x];
+        for (int w = 0; w < warp; ++w) row += warp_counts[w];
+        row += __popc(word & ((1u << lane) - 1u));
+        if (k < a.n_candidates && ((word >> lane) & 1u)) {
+            int64_t source, target;
+            long long shift[3];
+            T vec[3];
+            filter_candidate(a, k, source, target, shift, vec);
+            const int64_t s = source + a.index_offset, t = target + a.index_offset;
+            if (a.out_i) a.out_i[row] = s;
+            if (a.out_j) a.out_j[row] = t;
+            if (a.out_P) reinterpret_cast<longlong2*>(a.out_P)[row] = make_longlong2(s, t);
+            if (a.out_S) {
+                a.out_S[3 * row] = static_cast<int32_t>(shift[0]);
+                a.out_S[3 * row + 1] = static_cast<int32_t>(shift[1]);
+                a.out_S[3 * row + 2] = static_cast<int32_t>(shift[2]);
+            }
+            if (a.out_D) {
+                a.out_D[3 * row] = vec[0];
+                a.out_D[3 * row + 1] = vec[1];
+                a.out_D[3 * row + 2] = vec[2];
+            }
+            if (a.out_d) a.out_d[row] = pair_distance(vec[0], vec[1], vec[2]);
+        }
+    }
+}
+
 // Image tables of one structure per block: integer shifts enumerated x-major,
 // then y, then z (tonari csrc/core/geometry.cpp:229-237), and their Cartesian
 // translations in T.  Only the binning passes read the translations, both
@@ -1605,6 +1683,18 @@ thread_local int64_t g_kernel_launches = 0;
 }  // namespace
 
 int64_t launched_kernels() { return g_kernel_launches; }
+
+template <typename T>
+void launch_filter(const FilterArgs<T>& args, bool write, cudaStream_t stream) {
+    if (args.n_candidates == 0) return;
+    const unsigned blocks = static_cast<unsigned>(blocks_for(args.n_candidates, kFilterThreads));
+    if (write) {
+        filter_kernel<T, true><<<blocks, kFilterThreads, 0, stream>>>(args);
+    } else {
+        filter_kernel<T, false><<<blocks, kFilterThreads, 0, stream>>>(args);
+    }
+    ++g_kernel_launches;
+}
 
 template <typename T>
 void launch_geometry(const T* cell, const uint8_t* pbc, const int64_t* batch_ptr, int64_t batch,
@@ -1767,6 +1857,7 @@ void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* works
 
 #define TNR_INSTANTIATE(T)                                                                 \
     template void launch_prepare<T>(const PrepareArgs<T>&, cudaStream_t);                  \
+    template void launch_filter<T>(const FilterArgs<T>&, bool, cudaStream_t);              \
     template void launch_verify_wraps<T>(const T*, int64_t, const int32_t*, const T*,         \
                                          const int32_t*, uint32_t*, cudaStream_t);            \
     template void launch_geometry<T>(const T*, const uint8_t*, const int64_t*, int64_t, double, \

@@ -109,6 +109,35 @@ void launch_geometry(const T* cell, const uint8_t* pbc, const int64_t* batch_ptr
                      double cutoff, PrepareStructure<T>* prepare, DeviceGeometry* geometry,
                      uint32_t* flags, cudaStream_t stream);
 
+// Candidate-pair filter (Verlet-skin reuse): one bit per candidate, set when
+// its exact public-formula distance is below the cutoff.
+template <typename T>
+struct FilterArgs {
+    const T* positions;
+    const int64_t* batch_ptr;
+    int64_t batch;
+    const T* cell;              // (B,3,3)
+    const int64_t* pairs;       // (M,2), with index_offset
+    const int32_t* shifts;      // (M,3)
+    int64_t n_candidates;
+    int64_t index_offset;
+    T cutoff_squared;
+    uint32_t* keep_words;       // [ceil(M / 32)]
+    uint32_t* block_counts;     // [ceil(M / kFilterThreads)]
+    const int64_t* block_start; // scan of block_counts
+    int64_t* out_i;
+    int64_t* out_j;
+    int64_t* out_P;
+    int32_t* out_S;
+    T* out_d;
+    T* out_D;
+};
+
+constexpr int kFilterThreads = 256;
+
+template <typename T>
+void launch_filter(const FilterArgs<T>& args, bool write, cudaStream_t stream);
+
 // Sets *flag when any atom's wraps, recomputed with `duals` ([B][9] in T,
 // [cartesian][axis]), differ from `wraps`.
 template <typename T>

@@ -153,9 +153,76 @@ std::vector<at::Tensor> neighbor_list_cuda(const at::Tensor& positions, const at
     return outputs;
 }
 
+std::vector<at::Tensor> collect(TorchAllocator& context, const tnr_result& result,
+                                const at::TensorOptions& options, at::ScalarType real) {
+    const int64_t e = result.n_pairs;
+    std::vector<at::Tensor> outputs;
+    outputs.push_back(take(context, result.i, at::kLong, {result.i ? e : 0}, options));
+    outputs.push_back(take(context, result.j, at::kLong, {result.j ? e : 0}, options));
+    outputs.push_back(take(context, result.P, at::kLong, {result.P ? e : 0, 2}, options));
+    outputs.push_back(take(context, result.S, at::kInt, {result.S ? e : 0, 3}, options));
+    outputs.push_back(take(context, result.d, real, {result.d ? e : 0}, options));
+    outputs.push_back(take(context, result.D, real, {result.D ? e : 0, 3}, options));
+    outputs.push_back(take(context, result.edge_index, at::kLong, {2, result.edge_index ? e : 0}, options));
+    return outputs;
+}
+
+// Verlet-skin reuse: the candidate pairs (from a list built with cutoff +
+// skin) whose exact distance at the current positions is below `cutoff`.
+std::vector<at::Tensor> filter_pairs_cuda(const at::Tensor& positions, const at::Tensor& batch_ptr,
+                                          const at::Tensor& cell, const at::Tensor& pairs,
+                                          const at::Tensor& shifts, double cutoff,
+                                          std::string quantities, int64_t index_offset) {
+    TORCH_CHECK(positions.is_cuda() && batch_ptr.is_cuda() && cell.is_cuda() && pairs.is_cuda() &&
+                    shifts.is_cuda(),
+                "all inputs must be CUDA tensors");
+    TORCH_CHECK(positions.is_contiguous() && batch_ptr.is_contiguous() && cell.is_contiguous() &&
+                    pairs.is_contiguous() && shifts.is_contiguous(),
+                "all inputs must be contiguous");
+    TORCH_CHECK(positions.dim() == 2 && positions.size(1) == 3, "positions must have shape (N_total, 3)");
+    TORCH_CHECK(batch_ptr.dim() == 1 && batch_ptr.numel() > 1 && batch_ptr.scalar_type() == at::kLong,
+                "batch_ptr must be int64 with shape (B + 1,)");
+    TORCH_CHECK(cell.sizes() == at::IntArrayRef({batch_ptr.numel() - 1, 3, 3}) &&
+                    cell.scalar_type() == positions.scalar_type(),
+                "cell must have shape (B, 3, 3) and the dtype of positions");
+    TORCH_CHECK(pairs.dim() == 2 && pairs.size(1) == 2 && pairs.scalar_type() == at::kLong,
+                "pairs must be int64 with shape (M, 2)");
+    TORCH_CHECK(shifts.dim() == 2 && shifts.size(1) == 3 && shifts.size(0) == pairs.size(0) &&
+                    shifts.scalar_type() == at::kInt,
+                "shifts must be int32 with shape (M, 3)");
+    TORCH_CHECK(positions.scalar_type() == at::kFloat || positions.scalar_type() == at::kDouble,
+                "positions must have dtype float32 or float64");
+    const c10::cuda::CUDAGuard guard(positions.device());
+    const cudaStream_t stream = at::cuda::getCurrentCUDAStream(positions.get_device()).stream();
+    tnr_request request{};
+    request.dtype = positions.scalar_type() == at::kDouble ? TNR_FLOAT64 : TNR_FLOAT32;
+    request.n_atoms = positions.size(0);
+    request.n_structures = batch_ptr.numel() - 1;
+    request.positions = positions.data_ptr();
+    request.batch_ptr = batch_ptr.data_ptr<int64_t>();
+    request.cell = cell.data_ptr();
+    request.cutoff = cutoff;
+    request.quantities = parse_quantities(quantities);
+    request.index_offset = index_offset;
+    tnr_candidates candidates{pairs.data_ptr<int64_t>(), shifts.data_ptr<int32_t>(), pairs.size(0)};
+    TorchAllocator context{positions.device(), {}};
+    tnr_allocator allocator{&context, torch_allocate, torch_release};
+    tnr_result result{};
+    char message[512] = {0};
+    const int status = tnr_filter_pairs(&request, &candidates, &allocator,
+                                        reinterpret_cast<tnr_stream>(stream), &result, message,
+                                        sizeof(message));
+    TORCH_CHECK_VALUE(status != TNR_INPUT_ERROR, message);
+    TORCH_CHECK(status == TNR_OK, message);
+    return collect(context, result, positions.options(), positions.scalar_type());
+}
+
 }  // namespace
 
 TORCH_LIBRARY(tonari_b200, m) {
+    m.def(
+        "filter_pairs(Tensor positions, Tensor batch_ptr, Tensor cell, Tensor pairs, "
+        "Tensor shifts, float cutoff, str quantities, int index_offset) -> Tensor[]");
     m.def(
         "neighbor_list(Tensor positions, Tensor batch_ptr, Tensor cell, Tensor pbc, float cutoff, "
         "bool half_list, bool include_self, str algorithm, bool sorted, str quantities, "
@@ -164,4 +231,5 @@ TORCH_LIBRARY(tonari_b200, m) {
 
 TORCH_LIBRARY_IMPL(tonari_b200, CUDA, m) {
     m.impl("neighbor_list", &neighbor_list_cuda);
+    m.impl("filter_pairs", &filter_pairs_cuda);
 }
