@@ -55,7 +55,7 @@ def parse_args():
                         help="reduced size for profiling: atoms (cfg4) or structures (cfg2/3/5)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
-    parser.add_argument("--extra", default="cfg4",
+    parser.add_argument("--extra", default="cfg4,cfg2,cfg3",
                         help="comma list of extra configs measured at N=1 on rank 0")
     return parser.parse_args()
 
@@ -407,7 +407,7 @@ def main():
         extras = {}
         for name in filter(None, args.extra.split(",")):
             xw = make_workload(name, 0)
-            run = measure_device(xw, max(3, args.steps // 2), 2, device)
+            run = measure_device(xw, max(3, args.steps // 2), 3, device)
             ms = statistics.mean(run["step_ms"])
             extras[name] = {"pairs_per_s": run["n_pairs"] / (ms * 1e-3),
                             "structures_per_s": xw.n_structures / (ms * 1e-3),
