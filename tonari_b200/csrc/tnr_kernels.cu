@@ -408,23 +408,33 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
     const V q = reinterpret_cast<const V*>(args.wrapped)[atom];
     const int32_t wrap[3] = {args.wraps[3 * atom], args.wraps[3 * atom + 1],
                              args.wraps[3 * atom + 2]};
-    const int32_t center = (plan.n_images - 1) / 2;
-    const V* translations = reinterpret_cast<const V*>(args.image_translation) + plan.image_begin;
-    for (int32_t k = 0; k < plan.n_images; ++k) {
+    // The plan's fields live in registers for the image loop (the loop's
+    // atomics and stores would otherwise make the compiler reload them).
+    const int32_t n_images = plan.n_images;
+    const int32_t center = (n_images - 1) / 2;
+    const int64_t image_begin = plan.image_begin;
+    const int64_t bin_begin = plan.bin_begin;
+    const int32_t dims[3] = {plan.dims[0], plan.dims[1], plan.dims[2]};
+    const T lower[3] = {plan.lower[0], plan.lower[1], plan.lower[2]};
+    const T upper[3] = {plan.upper[0], plan.upper[1], plan.upper[2]};
+    const T origin[3] = {plan.origin[0], plan.origin[1], plan.origin[2]};
+    const T inv_edge = plan.inv_edge;
+    const V* translations = reinterpret_cast<const V*>(args.image_translation) + image_begin;
+    for (int32_t k = 0; k < n_images; ++k) {
         const V tr = translations[k];
         T g[3];
         g[0] = add_rn(q.x, tr.x);
         g[1] = add_rn(q.y, tr.y);
         g[2] = add_rn(q.z, tr.z);
-        const bool inside = g[0] >= plan.lower[0] && g[0] <= plan.upper[0] &&
-                            g[1] >= plan.lower[1] && g[1] <= plan.upper[1] &&
-                            g[2] >= plan.lower[2] && g[2] <= plan.upper[2];
+        const bool inside = g[0] >= lower[0] && g[0] <= upper[0] &&
+                            g[1] >= lower[1] && g[1] <= upper[1] &&
+                            g[2] >= lower[2] && g[2] <= upper[2];
         if (!inside && k != center) continue;
-        const int32_t bx = bin_axis(g[0], plan.origin[0], plan.inv_edge, plan.dims[0]);
-        const int32_t by = bin_axis(g[1], plan.origin[1], plan.inv_edge, plan.dims[1]);
-        const int32_t bz = bin_axis(g[2], plan.origin[2], plan.inv_edge, plan.dims[2]);
-        const int64_t bin = plan.bin_begin +
-            (static_cast<int64_t>(bx) * plan.dims[1] + by) * plan.dims[2] + bz;
+        const int32_t bx = bin_axis(g[0], origin[0], inv_edge, dims[0]);
+        const int32_t by = bin_axis(g[1], origin[1], inv_edge, dims[1]);
+        const int32_t bz = bin_axis(g[2], origin[2], inv_edge, dims[2]);
+        const int64_t bin = bin_begin +
+            (static_cast<int64_t>(bx) * dims[1] + by) * dims[2] + bz;
         const unsigned long long increment =
             k == center ? (1ull << 32) + 1ull : 1ull;
         const unsigned long long old = atomicAdd(&args.bin_counts[bin], increment);
@@ -448,7 +458,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
                 original.w = index_to_lane(static_cast<int32_t>(atom), T(0));
                 reinterpret_cast<V*>(args.ghost_orig)[slot] = original;
             }
-            const int4 image = args.image_shift[plan.image_begin + k];
+            const int4 image = args.image_shift[image_begin + k];
             args.ghost_meta[slot] = make_int4(image.x - wrap[0], image.y - wrap[1],
                                               image.z - wrap[2], static_cast<int32_t>(atom));
             if (k == center) {
