@@ -769,6 +769,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
         uint32_t* mask = args.mask_words + args.bin_word_start[bin];
         const T search2 = plan.search_squared;
         const T inner2 = plan.inner_squared;
+        const bool self_images = plan.self_images != 0;
         unsigned long long inner_pair = 0, search_pair = 0;
         if constexpr (std::is_same<T, float>::value) {
             inner_pair = pack2(inner2, inner2);
@@ -877,7 +878,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                     // key(c) == key(s) + 1: an image of source s itself, only
                     // possible where a lattice translation is shorter than the
                     // search radius; its shift decides it in the rare path.
-                    if (plan.self_images && (key & 1u) == 0u && key != 0u) {
+                    if (self_images && (key & 1u) == 0u && key != 0u) {
                         for (int r = 0; r < block; ++r) {
                             if (source_key[warp][r] == key) band_keys |= 1u << r;
                         }
