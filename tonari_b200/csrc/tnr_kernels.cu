@@ -1083,12 +1083,22 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
     const bool by_atom = args.source_order == 0;
     WriteShared<T>& sh = shared[warp];
     const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t bin = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-         bin < args.n_bins; bin += stride) {
-        const uint32_t first_source = static_cast<uint32_t>(args.bin_start[bin] >> 32);
-        const uint32_t n_bin_sources =
-            static_cast<uint32_t>(args.bin_start[bin + 1] >> 32) - first_source;
-        if (n_bin_sources == 0) continue;
+    // Bins probed 32 at a time, as in the count pass.
+    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         base < args.n_bins; base += 32 * stride) {
+      const int64_t my_bin = base + lane * stride;
+      uint32_t my_first = 0, my_count = 0;
+      if (my_bin < args.n_bins) {
+          my_first = static_cast<uint32_t>(args.bin_start[my_bin] >> 32);
+          my_count = static_cast<uint32_t>(args.bin_start[my_bin + 1] >> 32) - my_first;
+      }
+      unsigned pending = __ballot_sync(kFullMask, my_count != 0u);
+      while (pending != 0u) {
+        const int chosen = __ffs(pending) - 1;
+        pending &= pending - 1u;
+        const int64_t bin = base + chosen * stride;
+        const uint32_t first_source = __shfl_sync(kFullMask, my_first, chosen);
+        const uint32_t n_bin_sources = __shfl_sync(kFullMask, my_count, chosen);
         const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
         int32_t bx, by, bz;
         bin_coordinates(plan, bin, bx, by, bz);
@@ -1163,6 +1173,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
                 }
             }
         }
+      }
     }
 }
 
