@@ -36,6 +36,28 @@ def test_partition_is_contiguous_complete_and_balanced():
         assert max(loads) <= weights.sum() / n + weights.max() + 1e-6
 
 
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference CPU core not built")
+def test_pair_estimate_tracks_exact_counts_for_every_pbc_pattern():
+    """The balancing weight predicts each pbc group's pairs within a few percent
+    (non-periodic axes lose the spherical caps cut by the cell faces)."""
+    w = workloads.config5(n_structures=400)
+    w.pbc = np.asarray(w.pbc).copy()
+    w.pbc.reshape(-1, 3)[:20] = False  # finite cells with atoms inside, no periodic axis
+    pairs, _ = oracle.ref_neighbor_list(w.positions, w.cell, w.pbc, w.cutoff, w.batch_ptr,
+                                        half_list=True, algorithm="auto", threads=os.cpu_count() or 1)
+    source = np.asarray(pairs)[:, 0]
+    structure = np.searchsorted(w.batch_ptr, source, side="right") - 1
+    actual = np.bincount(structure, minlength=w.n_structures).astype(float)
+    counts = np.diff(w.batch_ptr)
+    estimate = sharding.estimate_pairs(w.batch_ptr, w.cell, w.pbc, w.cutoff, half_list=True)
+    estimate = estimate - sharding.kAtomWork * counts
+    periodic_axes = np.asarray(w.pbc).reshape(-1, 3).sum(axis=1)
+    for k in range(4):
+        group = periodic_axes == k
+        if group.sum() >= 5:
+            assert actual[group].sum() == pytest.approx(estimate[group].sum(), rel=0.08), k
+
+
 def test_partition_handles_more_shards_than_structures():
     batch_ptr = np.array([0, 5, 9], np.int64)
     shards = sharding.partition(batch_ptr, np.array([1.0, 1.0]), 4)
