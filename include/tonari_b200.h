@@ -120,16 +120,19 @@ int tnr_neighbor_list(const tnr_request* request, const tnr_allocator* allocator
 
 /*
  * No counterpart in the reference: an added entry point for callers that
- * cannot allocate device memory when they need a neighbor list (code in a
- * host callback, or a process whose GPU memory belongs to another allocator).
+ * cannot allocate device memory when they need a neighbor list -- a framework
+ * that forbids allocation on its hot path, or a process whose GPU memory is
+ * owned entirely by another allocator's pool, where a cudaMalloc would fail.
  * It allocates nothing: intermediates live in one fixed 8 MiB device array
  * per GPU that this library holds until the process exits, and the caller
  * passes the outputs.  Fill `result` with device pointers for every quantity
- * in request->quantities, each with room for `pair_capacity` pairs; on return
- * result->n_pairs is the pair count (also when it exceeded the capacity, which
- * returns TNR_ALLOC_ERROR and writes nothing).  At most 65536 atoms and 4096
- * structures per call (larger requests: TNR_INPUT_ERROR); every candidate is
- * enumerated, so it suits small systems, and request->algorithm is ignored.
+ * in request->quantities (a missing one is TNR_INPUT_ERROR), each with room
+ * for `pair_capacity` pairs; on return result->n_pairs is the pair count
+ * (also when it exceeded the capacity, which returns TNR_ALLOC_ERROR and
+ * writes nothing).  At most 65536 atoms and 4096 structures per call (larger
+ * requests: TNR_INPUT_ERROR); every candidate is enumerated, so it suits
+ * small systems, and request->algorithm is ignored.  All copies and kernels
+ * go on `stream`, and the call waits for `stream` to read the pair count.
  * The first call on a device looks up the array's address with that device
  * current -- make it before any stream capture.  All calls share the array:
  * calls that overlap on the GPU race, so serialise them.

@@ -43,3 +43,16 @@ def assert_same_pairs(actual_pairs, actual_shifts, expected_pairs, expected_shif
 def assert_sorted_by_source(pairs) -> None:
     source = to_numpy(pairs)[:, 0]
     assert np.all(source[1:] >= source[:-1])
+
+
+def expected_pairs(positions, cell, pbc, cutoff, batch_ptr=None, *, half_list=False,
+                   include_self=False):
+    """(pairs, shifts) from the reference's own CPU core (oracle/_ref) when it
+    was built, else from the plain-C restatement (oracle/_port)."""
+    from oracle import oracle
+
+    args = (to_numpy(positions), to_numpy(cell), to_numpy(pbc), cutoff,
+            None if batch_ptr is None else to_numpy(batch_ptr))
+    if oracle.ref_available():
+        return oracle.ref_neighbor_list(*args, half_list=half_list, include_self=include_self)
+    return oracle.port_neighbor_list(*args, half_list=half_list, include_self=include_self)

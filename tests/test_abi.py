@@ -68,6 +68,23 @@ def test_input_errors_are_reported_without_device_work():
     assert status == 1 and b"cutoff must be finite" in message.value
 
 
+def test_static_entry_point_checks_outputs_without_device_work():
+    # Output pointers and the capacity are checked before any device work, so
+    # a missing buffer is an input error rather than a device-side write.
+    lib = _cabi.library()
+    request = _cabi.Request(dtype=0, n_atoms=1, n_structures=1, cutoff=1.0,
+                            quantities=_cabi.quantity_mask("PS"))
+    result = _cabi.Result(P=16)
+    message = ctypes.create_string_buffer(256)
+    status = lib.tnr_neighbor_list_static(ctypes.byref(request), None, 8, ctypes.byref(result),
+                                          message, len(message))
+    assert status == 1 and b"result->S must be set" in message.value
+    result = _cabi.Result(P=16, S=16)
+    status = lib.tnr_neighbor_list_static(ctypes.byref(request), None, -1, ctypes.byref(result),
+                                          message, len(message))
+    assert status == 1 and b"pair_capacity must be nonnegative" in message.value
+
+
 def test_torch_op_registers():
     torch.ops.load_library(str(TORCH_LIBRARY))
     schema = str(torch.ops.tonari_b200.neighbor_list.default._schema)

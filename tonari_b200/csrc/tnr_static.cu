@@ -2,12 +2,13 @@
 // allocates device memory.
 //
 // Who needs it: callers that cannot call cudaMalloc at the moment they want a
-// neighbor list -- for example code running inside a host callback or a
-// framework that forbids allocation on its hot path, or an embedding whose
-// device memory is fully owned by another allocator.  They pass their input
-// and output buffers; every intermediate array lives in one fixed-size
-// device array owned by this library (kStaticScratchBytes, below), which each
-// GPU that loads the library keeps until the process exits.
+// neighbor list -- a framework that forbids allocation on its hot path, or an
+// embedding whose device memory is owned entirely by another allocator (a
+// memory pool that has reserved the GPU), where a cudaMalloc would fail or
+// fragment that pool.  They pass their input and output buffers; every
+// intermediate array lives in one fixed-size device array owned by this
+// library (kStaticScratchBytes, below), which each GPU that loads the library
+// keeps until the process exits.
 //
 // Limits and rules:
 //   * at most kStaticMaxAtoms atoms and kStaticMaxStructures structures per
@@ -17,6 +18,8 @@
 //   * the first call on a device looks up the scratch array's device address
 //     (cudaGetSymbolAddress) with that device current; make that first call
 //     before any stream capture;
+//   * the call waits for `stream` (it reads the pair count back) and issues
+//     all its copies and kernels on `stream`;
 //   * all calls share the one array and it keeps the previous call's
 //     contents, so calls that overlap on the GPU (different streams or host
 //     threads at the same time) race; serialise them.
@@ -104,8 +107,8 @@ void run_static(const tnr_request& request, cudaStream_t stream, int64_t capacit
     require_input(n_atoms <= kStaticMaxAtoms && batch <= kStaticMaxStructures,
                   "tnr_neighbor_list_static accepts at most 65536 atoms and 4096 structures");
 
-    // Host metadata: caller's host mirrors, else synchronous reads into
-    // ordinary host memory.
+    // Host metadata: caller's host mirrors, else reads on `stream` into
+    // ordinary host memory, complete once the stream has been synchronised.
     std::vector<int64_t> batch_ptr(static_cast<size_t>(batch + 1));
     std::vector<T> cell(static_cast<size_t>(9 * batch));
     std::vector<uint8_t> pbc(static_cast<size_t>(3 * batch));
@@ -114,15 +117,16 @@ void run_static(const tnr_request& request, cudaStream_t stream, int64_t capacit
         std::memcpy(cell.data(), request.cell_host, cell.size() * sizeof(T));
         std::memcpy(pbc.data(), request.pbc_host, pbc.size());
     } else {
-        check(cudaStreamSynchronize(stream), "synchronise");
-        check(cudaMemcpy(batch_ptr.data(), request.batch_ptr, batch_ptr.size() * sizeof(int64_t),
-                         cudaMemcpyDeviceToHost), "read batch_ptr");
+        check(cudaMemcpyAsync(batch_ptr.data(), request.batch_ptr,
+                              batch_ptr.size() * sizeof(int64_t), cudaMemcpyDeviceToHost, stream),
+              "read batch_ptr");
         if (batch) {
-            check(cudaMemcpy(cell.data(), request.cell, cell.size() * sizeof(T),
-                             cudaMemcpyDeviceToHost), "read cell");
-            check(cudaMemcpy(pbc.data(), request.pbc, pbc.size(), cudaMemcpyDeviceToHost),
-                  "read pbc");
+            check(cudaMemcpyAsync(cell.data(), request.cell, cell.size() * sizeof(T),
+                                  cudaMemcpyDeviceToHost, stream), "read cell");
+            check(cudaMemcpyAsync(pbc.data(), request.pbc, pbc.size(), cudaMemcpyDeviceToHost,
+                                  stream), "read pbc");
         }
+        check(cudaStreamSynchronize(stream), "read metadata");
     }
     require_input(batch_ptr[0] == 0, "batch_ptr must start at zero");
     require_input(batch_ptr[batch] == n_atoms, "batch_ptr must end at N_total");
@@ -196,23 +200,20 @@ void run_static(const tnr_request& request, cudaStream_t stream, int64_t capacit
     auto* d_status = carve.take<uint32_t>(4);
     void* d_scan = carve.take<unsigned char>(scan_workspace_bytes(n_atoms));
 
-    // Uploads from ordinary host memory are complete when cudaMemcpy returns,
-    // so the host vectors may go out of scope afterwards.
-    check(cudaStreamSynchronize(stream), "synchronise");
-    check(cudaMemcpy(d_prepare, prepare.data(), prepare.size() * sizeof(prepare[0]),
-                     cudaMemcpyHostToDevice), "upload");
-    check(cudaMemcpy(d_plans, plans.data(), plans.size() * sizeof(plans[0]),
-                     cudaMemcpyHostToDevice), "upload");
-    check(cudaMemcpy(d_reductions, reductions.data(), reductions.size() * sizeof(reductions[0]),
-                     cudaMemcpyHostToDevice), "upload");
-    if (!brute_structs.empty()) {
-        check(cudaMemcpy(d_brute_structs, brute_structs.data(),
-                         brute_structs.size() * sizeof(int32_t), cudaMemcpyHostToDevice), "upload");
-    }
-    check(cudaMemcpy(d_brute_prefix, brute_prefix.data(), brute_prefix.size() * sizeof(int64_t),
-                     cudaMemcpyHostToDevice), "upload");
-    check(cudaMemcpy(d_image_shift, image_shift.data(), image_shift.size() * sizeof(int4),
-                     cudaMemcpyHostToDevice), "upload");
+    // Uploads are ordered on `stream` before the kernels that read them.  The
+    // host vectors stay alive until the stream is synchronised for the pair
+    // total below, after the last upload has completed.
+    auto upload = [stream](void* destination, const void* source, size_t bytes) {
+        if (bytes == 0) return;
+        check(cudaMemcpyAsync(destination, source, bytes, cudaMemcpyHostToDevice, stream),
+              "upload");
+    };
+    upload(d_prepare, prepare.data(), prepare.size() * sizeof(prepare[0]));
+    upload(d_plans, plans.data(), plans.size() * sizeof(plans[0]));
+    upload(d_reductions, reductions.data(), reductions.size() * sizeof(reductions[0]));
+    upload(d_brute_structs, brute_structs.data(), brute_structs.size() * sizeof(int32_t));
+    upload(d_brute_prefix, brute_prefix.data(), brute_prefix.size() * sizeof(int64_t));
+    upload(d_image_shift, image_shift.data(), image_shift.size() * sizeof(int4));
     // Scratch keeps the previous call's bytes: clear what must start at zero.
     check(cudaMemsetAsync(d_status, 0, 4 * sizeof(uint32_t), stream), "clear status");
     check(cudaMemsetAsync(d_counts, 0, n_atoms * sizeof(uint32_t), stream), "clear counts");
@@ -303,6 +304,14 @@ extern "C" int tnr_neighbor_list_static(const tnr_request* request, tnr_stream s
                       "positions must have dtype float32 or float64");
         require_input(!(request->quantities & TNR_Q_EDGE),
                       "edge_index is not offered by the allocation-free entry point");
+        require_input(pair_capacity >= 0, "pair_capacity must be nonnegative");
+        const uint32_t q = request->quantities;
+        require_input(!(q & TNR_Q_I) || result->i, "result->i must be set when i is requested");
+        require_input(!(q & TNR_Q_J) || result->j, "result->j must be set when j is requested");
+        require_input(!(q & TNR_Q_P) || result->P, "result->P must be set when P is requested");
+        require_input(!(q & TNR_Q_S) || result->S, "result->S must be set when S is requested");
+        require_input(!(q & TNR_Q_d) || result->d, "result->d must be set when d is requested");
+        require_input(!(q & TNR_Q_D) || result->D, "result->D must be set when D is requested");
         if (request->dtype == TNR_FLOAT32) {
             run_static<float>(*request, stream, pair_capacity, *result);
         } else {
