@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.support import canonical
+from tests.support import canonical, expected_pairs
 from tonari_b200 import neighbor_graph, neighbor_list
 
 
@@ -49,6 +49,9 @@ def test_edge_index_matches_neighbor_list(dtype, half_list):
     rows = canonical(edge_index.T, shifts)
     ref_rows = canonical(pairs, ref_shifts)
     assert np.array_equal(rows, ref_rows)
+    oracle_rows = canonical(*expected_pairs(positions, cell, pbc, 3.0, batch_ptr,
+                                            half_list=half_list))
+    assert np.array_equal(rows, oracle_rows)
     key = lambda p, s: np.lexsort(tuple(np.concatenate((p, s), 1)[:, k] for k in range(4, -1, -1)))
     order = key(edge_index.T.cpu().numpy(), shifts.cpu().numpy().astype(np.int64))
     ref_order = key(pairs.cpu().numpy(), ref_shifts.cpu().numpy().astype(np.int64))

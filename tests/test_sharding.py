@@ -146,3 +146,13 @@ def test_gloo_shard_failure_reaches_every_rank():
     assert "cell must contain only finite values" in by_rank[1][3]
     assert by_rank[0][1] == "error" and by_rank[0][2] == "ShardFailure"
     assert "rank 1" in by_rank[0][3]
+
+
+def test_shard_rejects_unknown_options():
+    # With the default provider, an option it does not know is an error, not
+    # silently dropped.
+    w = workloads.config2(n_structures=4)
+    shard = sharding.partition(w.batch_ptr, np.ones(4), 1)[0]
+    with pytest.raises(TypeError, match="half_lst"):
+        sharding.neighbor_list_shard("PS", shard, w.positions, w.cell, w.pbc, w.cutoff,
+                                     w.batch_ptr, half_lst=True)

@@ -1,6 +1,6 @@
 """Verlet-skin reuse (VerletNeighborList, tnr_filter_pairs): between
-rebuilds the filtered candidates must be the same pair set as a fresh
-neighbor_list at the cutoff (bit-exact keys, d/D within the usual
+rebuilds the filtered candidates must be the reference CPU core's pair set at
+the cutoff on the current positions, and the same as a fresh neighbor_list (bit-exact keys, d/D within the usual
 tolerances), and rebuilds must happen when atoms move too far or the cell
 changes."""
 from __future__ import annotations
@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.support import assert_same_pairs, assert_sorted_by_source
+from tests.support import assert_same_pairs, assert_sorted_by_source, expected_pairs
 from tonari_b200 import VerletNeighborList, neighbor_list
 
 
@@ -50,6 +50,9 @@ def test_trajectory_matches_fresh_lists(dtype, half_list):
         ref_pairs, ref_shifts, ref_D = neighbor_list("PSD", positions, cell, pbc, 3.5, batch_ptr,
                                                      half_list=half_list, sorted=True)
         assert_sorted_by_source(pairs)
+        # The pair set is the reference CPU core's on the moved positions.
+        assert_same_pairs(pairs, shifts, *expected_pairs(positions, cell, pbc, 3.5, batch_ptr,
+                                                         half_list=half_list))
         assert_same_pairs(pairs, shifts, ref_pairs, ref_shifts)
         # Both are source-major; within a source compare after the canonical sort.
         order = np.lexsort(tuple(np.concatenate((pairs.cpu().numpy(), shifts.cpu().numpy()), 1)[:, k]

@@ -116,11 +116,16 @@ def neighbor_list_shard(quantities: str, shard: Shard, positions, cell, pbc, cut
     if neighbor_list is None:
         from ._frontend import neighbor_list_torch
 
+        algorithm = options.pop("algorithm", "auto")
+        sort = options.pop("sorted", False)
+        half_list = options.pop("half_list", False)
+        include_self = options.pop("include_self", False)
+        if options:
+            raise TypeError(f"unexpected neighbor-list options: {sorted(options)}")
         return neighbor_list_torch(
             quantities, sub[0], sub[1], sub[2], cutoff, sub[3],
-            algorithm=options.pop("algorithm", "auto"), cpu_threads=None,
-            sorted=options.pop("sorted", False), half_list=options.pop("half_list", False),
-            include_self=options.pop("include_self", False), index_offset=shard.atom_begin)
+            algorithm=algorithm, cpu_threads=None, sorted=sort, half_list=half_list,
+            include_self=include_self, index_offset=shard.atom_begin)
     return neighbor_list(quantities, sub[0], sub[1], sub[2], cutoff, sub[3],
                          index_offset=shard.atom_begin, **options)
 
