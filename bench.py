@@ -4,24 +4,28 @@
     python bench.py --impl reference ...     # reference CPU arm
 
 Workload (default cfg5, tonari_b200/workloads.py): 8192 triclinic structures,
-50-5000 atoms, mixed pbc, float32, cutoff 5, half list, 'PS'.  Scaling is
-weak: with N ranks the global batch is N seeded cfg5 batches, split into N
-contiguous shards balanced by estimated pair count (tonari_b200.sharding);
-no collective on the data path; value = pairs of all ranks / max-over-ranks
-time.
+50-5000 atoms, mixed pbc, float32, cutoff 5, half list, 'PS'.
 
-A step is one neighbor_list call over the whole batch.
+Scaling is strong by default: with N ranks the one cfg5 batch is split into N
+contiguous shards balanced by estimated pair count (tonari_b200.sharding);
+each rank searches its shard with globally numbered indices and keeps its
+pairs; there is no collective on the data path.  value = the batch's pairs /
+max-over-ranks time.  At N>1 the weak-scaling figure (N seeded copies of the
+batch, one per rank) is measured as well and reported under "weak".
+
+A step is one neighbor_list call over the rank's shard.
 * value: inputs already in HBM, device time per step from CUDA events on the
   launching stream; L2 is flushed (256 MiB write) between steps, outside the
   events.
 * e2e: the same call from pinned host inputs: H2D of positions/cell/pbc/
   batch_ptr, the call, and D2H of every output into pinned host memory.
 * roofline: algorithmic bytes (inputs read once + requested outputs written
-  once) over the write-pass kernel time measured by the library's phase
-  events during the timed steps, against MEASURED_PEAKS.json hbm_gbs; the
-  whole-call fraction is reported as call_frac.
-* cpu_baseline: the reference CPU core (oracle/_ref, else the C port) on a
-  bounded sample of the same workload, all host cores, rank 0 at N=1 only.
+  once) over the device time of the dominant phase (the library's phase
+  events, which bracket exactly that phase's kernel launches), against
+  MEASURED_PEAKS.json hbm_gbs; the write pass and the whole call are reported
+  beside it.
+* cpu_baseline: the reference CPU core (oracle/_ref, else the C port) on the
+  whole workload, one thread per physical core, rank 0 at N=1 only.
 """
 from __future__ import annotations
 
@@ -55,6 +59,7 @@ def parse_args():
                         help="reduced size for profiling: atoms (cfg4) or structures (cfg2/3/5)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--scaling", choices=["strong", "weak"], default="strong")
     parser.add_argument("--extra", default="cfg4,cfg2,cfg3",
                         help="comma list of extra configs measured at N=1 on rank 0")
     return parser.parse_args()
@@ -74,24 +79,42 @@ SIZE_KEYWORD = {"cfg2": "n_structures", "cfg3": "n_structures", "cfg4": "n_atoms
                 "cfg5": "n_structures"}
 
 
-def make_workload(name: str, rank: int, world: int = 1, size: int | None = None):
-    """The rank's share of the job.  N=1: the configuration itself.  N>1
-    (weak scaling): the global batch is N seeded copies of the configuration
-    (seeds s, s+1, ...), split into N contiguous shards balanced by estimated
-    pair count (tonari_b200.sharding); a single structure is never split."""
+def make_workload(name: str, rank: int, world: int = 1, size: int | None = None,
+                  scaling: str = "strong"):
+    """The rank's share of the job.  N=1: the configuration itself.  N>1,
+    strong: the configuration's batch split into N contiguous shards balanced
+    by estimated pair count (tonari_b200.sharding); weak: the global batch is
+    N seeded copies of the configuration (seeds s, s+1, ...), split the same
+    way.  A single structure is never split: it is replicated."""
     from tonari_b200 import sharding, workloads
 
     extra = {SIZE_KEYWORD[name]: size} if size else {}
     if world == 1:
         return workloads.CONFIGS[name](seed=SEEDS[name], **extra)
-    parts = [workloads.CONFIGS[name](seed=SEEDS[name] + k, **extra) for k in range(world)]
-    whole = workloads.concatenate(parts, f"{name}x{world}")
+    copies = world if scaling == "weak" else 1
+    parts = [workloads.CONFIGS[name](seed=SEEDS[name] + k, **extra) for k in range(copies)]
+    whole = parts[0] if copies == 1 else workloads.concatenate(parts, f"{name}x{world}")
+    if whole.n_structures == 1:
+        return whole
     weights = sharding.estimate_pairs(whole.batch_ptr, whole.cell, whole.pbc, whole.cutoff,
                                       half_list=whole.options.get("half_list", False))
     shard = sharding.partition(whole.batch_ptr, weights, world)[rank]
     part = whole.shard(shard.structure_begin, shard.structure_end)
-    part.name = f"{name}x{world}[rank {rank}]"
+    part.name = f"{whole.name}[rank {rank} of {world}]"
     return part
+
+
+def physical_cores() -> int:
+    """Physical cores of this host (unique core/socket pairs from lscpu)."""
+    try:
+        text = subprocess.run(["lscpu", "-p=CORE,SOCKET"], capture_output=True, text=True,
+                              check=True).stdout
+        cores = {line for line in text.splitlines() if line and not line.startswith("#")}
+        if cores:
+            return len(cores)
+    except (OSError, subprocess.CalledProcessError):
+        pass
+    return os.cpu_count() or 1
 
 
 def call_kwargs(w):
@@ -155,13 +178,24 @@ def core_library():
     lib.tnr_last_launch_count.restype = ctypes.c_int64
     lib.tnr_last_phase_times.restype = ctypes.c_int
     lib.tnr_last_phase_times.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_int]
+    lib.tnr_last_host_times.restype = ctypes.c_int
+    lib.tnr_last_host_times.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_int]
     return lib
+
+
+PHASES = ("prepare", "bin", "count", "scan", "readback", "write")
 
 
 def phase_times(lib):
     buffer = (ctypes.c_float * 6)()
     lib.tnr_last_phase_times(buffer, 6)
     return list(buffer)
+
+
+def host_times(lib):
+    buffer = (ctypes.c_double * 12)()
+    lib.tnr_last_host_times(buffer, 12)
+    return list(buffer)[:9]
 
 
 def measure_device(w, steps, warmup, device):
@@ -180,7 +214,7 @@ def measure_device(w, steps, warmup, device):
         del out
     torch.cuda.synchronize(device)
     os.environ["TONARI_B200_PHASE_TIMERS"] = "1"
-    step_ms, write_ms, launches, n_pairs = [], [], [], 0
+    step_ms, phases, hosts, launches, n_pairs = [], [], [], [], 0
     try:
         for _ in range(steps):
             flush.zero_()
@@ -191,13 +225,17 @@ def measure_device(w, steps, warmup, device):
             end.record(stream)
             end.synchronize()
             step_ms.append(start.elapsed_time(end))
-            write_ms.append(phase_times(lib)[5])
+            phases.append(phase_times(lib))
+            hosts.append(host_times(lib))
             launches.append(int(lib.tnr_last_launch_count()))
             n_pairs = int(out[0].shape[0])
             del out
     finally:
         os.environ.pop("TONARI_B200_PHASE_TIMERS", None)
-    return {"step_ms": step_ms, "write_ms": write_ms, "launches": launches, "n_pairs": n_pairs}
+    median_phase = [statistics.median(p[k] for p in phases) for k in range(6)]
+    median_host = [statistics.median(h[k] for h in hosts) for k in range(9)]
+    return {"step_ms": step_ms, "phase_ms": median_phase, "host_ms": median_host,
+            "launches": launches, "n_pairs": n_pairs}
 
 
 def measure_e2e(w, steps, warmup, device):
@@ -230,69 +268,62 @@ def measure_e2e(w, steps, warmup, device):
     return {"step_ms": times, "h2d": h2d, "d2h": d2h}
 
 
-def cpu_reference_rate(w, max_seconds=3.0):
-    """Reference CPU core on a bounded sample of the workload (first structures,
-    growing until one run takes about max_seconds).  Returns a dict."""
+def cpu_reference_rate(w, threads=None):
+    """Reference CPU core (oracle/_ref; the C port when it was not built) on
+    the whole workload, one thread per physical core.  Returns a dict."""
     from oracle import oracle
 
-    threads = os.cpu_count() or 1
+    threads = threads or physical_cores()
     kind = "reference" if oracle.ref_available() else "port"
-    b = w.n_structures
-    count = max(1, b // 64) if b > 1 else 1
-    while True:
-        sample = w.shard(0, count) if b > 1 else w
-        start = time.perf_counter()
-        if kind == "reference":
-            pairs, _ = oracle.ref_neighbor_list(
-                sample.positions, sample.cell, sample.pbc, sample.cutoff, sample.batch_ptr,
-                half_list=w.options.get("half_list", False),
-                algorithm=w.options.get("algorithm", "auto"), threads=threads)
-        else:
-            pairs, _ = oracle.port_neighbor_list(
-                sample.positions, sample.cell, sample.pbc, sample.cutoff, sample.batch_ptr,
-                half_list=w.options.get("half_list", False))
-            threads = 1
-        seconds = time.perf_counter() - start
-        if seconds >= max_seconds or count >= b or kind == "port":
-            break
-        count = min(b, max(count + 1, int(count * max_seconds / max(seconds, 1e-3))))
+    start = time.perf_counter()
+    if kind == "reference":
+        pairs, _ = oracle.ref_neighbor_list(
+            w.positions, w.cell, w.pbc, w.cutoff, w.batch_ptr,
+            half_list=w.options.get("half_list", False),
+            algorithm=w.options.get("algorithm", "auto"), threads=threads)
+    else:
+        pairs, _ = oracle.port_neighbor_list(
+            w.positions, w.cell, w.pbc, w.cutoff, w.batch_ptr,
+            half_list=w.options.get("half_list", False))
+        threads = 1
+    seconds = time.perf_counter() - start
     return {"value": len(pairs) / seconds, "unit": "pairs/s", "cores": threads, "kind": kind,
-            "sample": f"{w.name} structures [0,{count}) of {b}: {sample.n_atoms} atoms, "
-                      f"{len(pairs)} pairs in {seconds:.2f} s",
-            "structures_per_s": count / seconds}
+            "sample": f"{w.name}: all {w.n_structures} structures, {w.n_atoms} atoms, "
+                      f"{len(pairs)} pairs in {seconds:.2f} s ({threads} threads = physical "
+                      f"cores from lscpu)",
+            "structures_per_s": w.n_structures / seconds}
 
 
-def measured_traffic_per_pair():
-    """Write-kernel DRAM bytes per emitted pair from the committed ncu summary
-    (profiles/traffic_cfg5_1024.md), or None."""
-    path = ROOT / "profiles" / "traffic_cfg5_1024.md"
-    if path.exists():
-        for line in path.read_text().splitlines():
-            if line.startswith("write_kernel_traffic_bytes_per_pair:"):
-                return float(line.split(":")[1])
-    return None
+# DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
+# captures summarised in profiles/ (the capture command is in each summary),
+# per emitted pair, keyed by (workload, phase).
+TRAFFIC_PER_PAIR = {}
 
 
-def roofline(w, n_pairs, write_ms, step_ms):
+def roofline(w, n_pairs, phase_ms, step_ms):
     from tonari_b200.workloads import algorithmic_bytes
 
     peak, source = peak_hbm()
-    traffic_bytes = algorithmic_bytes(w, n_pairs)
-    achieved = traffic_bytes / (write_ms * 1e-3) / 1e9
-    per_pair = measured_traffic_per_pair() if w.name.startswith("cfg5") else None
-    traffic = int(per_pair * n_pairs) if per_pair else None
-    traffic_source = ("ncu dram read+write of cell_emit_kernel on cfg5[:1024], scaled by pairs "
-                      "(profiles/traffic_cfg5_1024.md)" if traffic else None)
-    call = traffic_bytes / (step_ms * 1e-3) / 1e9
+    algorithmic = algorithmic_bytes(w, n_pairs)
+    kernel_phases = [k for k in range(6) if PHASES[k] != "readback"]
+    dominant = max(kernel_phases, key=lambda k: phase_ms[k])
+    achieved = algorithmic / (phase_ms[dominant] * 1e-3) / 1e9
+    write = algorithmic / (phase_ms[5] * 1e-3) / 1e9 if phase_ms[5] > 0 else None
+    call = algorithmic / (step_ms * 1e-3) / 1e9
+    per_pair = TRAFFIC_PER_PAIR.get((w.name.split("[")[0], PHASES[dominant]))
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": f"{source} hbm_gbs",
-            "kernel": "cell/brute write pass", "algorithmic_bytes": traffic_bytes,
-            "traffic": traffic, "traffic_source": traffic_source,
+            "kernel": f"{PHASES[dominant]} phase", "kernel_ms": round(phase_ms[dominant], 4),
+            "algorithmic_bytes": algorithmic,
+            "traffic": int(per_pair * n_pairs) if per_pair else None,
+            "phase_ms": {PHASES[k]: round(phase_ms[k], 4) for k in range(6)},
+            "write_frac": round(write / peak, 4) if write else None,
             "call_achieved": round(call, 1), "call_frac": round(call / peak, 4)}
 
 
 def run_reference(args):
-    """Reference arm: the reference's CPU implementation, all host cores."""
+    """Reference arm: the reference's CPU implementation on the whole
+    workload, one thread per physical core; rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -301,7 +332,7 @@ def run_reference(args):
     w = make_workload(args.workload, 0, 1, args.size)
     rates, samples = [], None
     for step in range(args.warmup + args.steps):
-        result = cpu_reference_rate(w, max_seconds=1.0)
+        result = cpu_reference_rate(w)
         if step >= args.warmup:
             rates.append(result["value"])
             samples = result
@@ -309,7 +340,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "pairs/s", "value": value, "unit": "pairs/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "f32" if w.positions.dtype == np.float32 else "f64", "data": "synthetic",
         "config": {"workload": w.name, "structures": w.n_structures, "atoms": w.n_atoms,
                    "cutoff": w.cutoff, "quantities": w.quantities, **call_kwargs(w)},
@@ -319,6 +350,7 @@ def run_reference(args):
                 "d2h_bytes_per_step": 0},
         "structures_per_s": samples["structures_per_s"],
         "reference_available": oracle.ref_available(),
+        "same_config": True,
     }
     print(json.dumps(line), flush=True)
 
@@ -342,7 +374,9 @@ def main():
 
     load_torch_cuda()
 
-    w = make_workload(args.workload, rank, world, args.size)
+    w = make_workload(args.workload, rank, world, args.size, args.scaling)
+    replicas = world > 1 and w.n_structures == 1
+    scaling = "weak" if (args.scaling == "weak" or replicas) else "strong"
 
     def barrier():
         if world > 1:
@@ -363,6 +397,13 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
+    def gather(obj):
+        if world == 1:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
     barrier()
     with Clocks(local_rank) as clocks:
         device_run = measure_device(w, args.steps, args.warmup, device)
@@ -372,6 +413,25 @@ def main():
     pairs_all = sum_over_ranks(device_run["n_pairs"])
     structures_all = sum_over_ranks(w.n_structures)
     value = pairs_all / (ms_per_step * 1e-3)
+    per_rank = gather({
+        "rank": rank, "structures": w.n_structures, "atoms": w.n_atoms,
+        "pairs": device_run["n_pairs"],
+        "ms_per_step": round(statistics.mean(device_run["step_ms"]), 4),
+        "phase_ms": {PHASES[k]: round(v, 4) for k, v in enumerate(device_run["phase_ms"])},
+        "host_marks_ms": [round(v, 3) for v in device_run["host_ms"]],
+    })
+
+    weak = None
+    if world > 1 and scaling == "strong":
+        ww = make_workload(args.workload, rank, world, args.size, "weak")
+        barrier()
+        weak_run = measure_device(ww, args.steps, args.warmup, device)
+        barrier()
+        weak_ms = max_over_ranks(sum(weak_run["step_ms"])) / args.steps
+        weak_pairs = sum_over_ranks(weak_run["n_pairs"])
+        weak = {"value": weak_pairs / (weak_ms * 1e-3), "unit": "pairs/s",
+                "ms_per_step": weak_ms, "pairs_per_step": int(weak_pairs),
+                "workload": f"{args.workload} x{world} (seeded copies, one batch per rank)"}
 
     e2e = None
     if not args.no_e2e:
@@ -383,24 +443,38 @@ def main():
                "h2d_bytes_per_step": int(sum_over_ranks(e2e_run["h2d"])),
                "d2h_bytes_per_step": int(sum_over_ranks(e2e_run["d2h"]))}
 
-    write_ms = statistics.median(device_run["write_ms"])
+    if world == 1:
+        workload_name = args.workload
+        parallelism = "1 GPU"
+    elif replicas:
+        workload_name = f"{args.workload} (one structure, replicated on {world} GPUs)"
+        parallelism = f"{world} replicas, no data-path collective"
+    else:
+        workload_name = (f"{args.workload} split into {world} shards" if scaling == "strong"
+                         else f"{args.workload} x{world}")
+        parallelism = f"{world} ranks, contiguous shards, no data-path collective"
     line = {
         "metric": "pairs/s", "value": value, "unit": "pairs/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "f32" if w.positions.dtype == np.float32 else "f64", "data": "synthetic",
-        "config": {"workload": args.workload if world == 1 else f"{args.workload} x{world}",
-                   "structures_per_gpu": w.n_structures,
-                   "atoms_per_gpu": w.n_atoms, "cutoff": w.cutoff, "quantities": w.quantities,
-                   **call_kwargs(w), "pairs_per_step": int(pairs_all),
+        "config": {"workload": workload_name,
+                   "structures_per_step": int(structures_all),
+                   "atoms_per_step": int(sum_over_ranks(w.n_atoms)), "cutoff": w.cutoff,
+                   "quantities": w.quantities, **call_kwargs(w),
+                   "pairs_per_step": int(pairs_all),
                    "l2": "flushed between steps (256 MiB write)",
-                   "parallelism": f"{world} independent ranks, no data-path collective"},
+                   "parallelism": parallelism},
         "structures_per_s": structures_all / (ms_per_step * 1e-3),
-        "gpu_launches": int(sum(device_run["launches"])),
-        "roofline": roofline(w, device_run["n_pairs"], write_ms, ms_per_step),
+        "gpu_launches": int(sum_over_ranks(sum(device_run["launches"]))),
+        "roofline": roofline(w, device_run["n_pairs"], device_run["phase_ms"],
+                             statistics.mean(device_run["step_ms"])),
         "clocks": clocks.summary(),
         "e2e": e2e,
+        "ranks": per_rank,
     }
+    if weak is not None:
+        line["weak"] = weak
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_reference_rate(w)
     if rank == 0 and world == 1 and args.extra:
@@ -412,8 +486,8 @@ def main():
             extras[name] = {"pairs_per_s": run["n_pairs"] / (ms * 1e-3),
                             "structures_per_s": xw.n_structures / (ms * 1e-3),
                             "ms_per_step": ms, "pairs": run["n_pairs"],
-                            "roofline": roofline(xw, run["n_pairs"],
-                                                 statistics.median(run["write_ms"]), ms)}
+                            "host_marks_ms": [round(v, 3) for v in run["host_ms"]],
+                            "roofline": roofline(xw, run["n_pairs"], run["phase_ms"], ms)}
         line["extra_configs"] = extras
     if rank == 0:
         print(json.dumps(line), flush=True)
