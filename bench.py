@@ -60,6 +60,9 @@ def parse_args():
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--scaling", choices=["strong", "weak"], default="strong")
+    parser.add_argument("--reference-cuda", default="cfg5,cfg4",
+                        help="configs on which the reference's own CUDA provider (baseline/_ref) "
+                             "is timed as a GPU comparator at N=1; empty to skip")
     parser.add_argument("--extra", default="cfg4,cfg2,cfg3",
                         help="comma list of extra configs measured at N=1 on rank 0")
     return parser.parse_args()
@@ -183,7 +186,7 @@ def core_library():
     return lib
 
 
-PHASES = ("prepare", "bin", "count", "scan", "readback", "write")
+PHASES = ("prepare", "bin", "search", "scan", "readback", "write")
 
 
 def phase_times(lib):
@@ -308,7 +311,9 @@ def roofline(w, n_pairs, phase_ms, step_ms):
     kernel_phases = [k for k in range(6) if PHASES[k] != "readback"]
     dominant = max(kernel_phases, key=lambda k: phase_ms[k])
     achieved = algorithmic / (phase_ms[dominant] * 1e-3) / 1e9
-    write = algorithmic / (phase_ms[5] * 1e-3) / 1e9 if phase_ms[5] > 0 else None
+    # One-pass calls emit inside the search phase; the write phase then only
+    # exists for two-pass (sorted) calls.
+    write = algorithmic / (phase_ms[5] * 1e-3) / 1e9 if phase_ms[5] > 0.01 else None
     call = algorithmic / (step_ms * 1e-3) / 1e9
     per_pair = TRAFFIC_PER_PAIR.get((w.name.split("[")[0], PHASES[dominant]))
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -319,6 +324,49 @@ def roofline(w, n_pairs, phase_ms, step_ms):
             "phase_ms": {PHASES[k]: round(phase_ms[k], 4) for k in range(6)},
             "write_frac": round(write / peak, 4) if write else None,
             "call_achieved": round(call, 1), "call_frac": round(call / peak, 4)}
+
+
+def reference_cuda_rate(name, steps, warmup, device):
+    """The reference's stock CUDA path on this GPU, as a comparator: the
+    unmodified reference package from baseline/_ref, its public
+    tonari.neighbor_list on CUDA tensors (its own provider and frontend), with
+    the same inputs, options and timing rules as `value`."""
+    import torch
+
+    site = ROOT / "baseline" / "_ref"
+    if not (site / "tonari" / "api.py").exists():
+        return {"unavailable": "the reference package is not installed in baseline/_ref"}
+    sys.path.insert(0, str(site))
+    try:
+        import tonari
+    finally:
+        sys.path.remove(str(site))
+    w = make_workload(name, 0)
+    positions, cell, pbc, batch_ptr = w.torch_inputs(device)
+    kwargs = call_kwargs(w)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    times, n_pairs = [], 0
+    try:
+        for step in range(warmup + steps):
+            flush.zero_()
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            out = tonari.neighbor_list(w.quantities, positions, cell, pbc, w.cutoff, batch_ptr,
+                                       **kwargs)
+            end.record(stream)
+            end.synchronize()
+            if step >= warmup:
+                times.append(start.elapsed_time(end))
+            n_pairs = int(out[0].shape[0])
+            del out
+    except (RuntimeError, ValueError) as error:
+        return {"unavailable": f"the reference CUDA provider failed: {str(error)[:200]}"}
+    ms = statistics.mean(times)
+    return {"pairs_per_s": n_pairs / (ms * 1e-3), "structures_per_s": w.n_structures / (ms * 1e-3),
+            "ms_per_step": ms, "pairs": n_pairs, "steps": steps, "warmup": warmup,
+            "path": "baseline/_ref tonari.neighbor_list on CUDA tensors (reference CUDA provider)"}
 
 
 def run_reference(args):
@@ -489,6 +537,13 @@ def main():
                             "host_marks_ms": [round(v, 3) for v in run["host_ms"]],
                             "roofline": roofline(xw, run["n_pairs"], run["phase_ms"], ms)}
         line["extra_configs"] = extras
+    if rank == 0 and world == 1 and args.reference_cuda:
+        # The reference's CUDA path takes about 15 s per cfg5 call on a B200:
+        # one warm-up and one timed call there, three of each elsewhere.
+        line["reference_cuda"] = {
+            name: reference_cuda_rate(name, 1 if name == "cfg5" else 3, 1 if name == "cfg5" else 2,
+                                      device)
+            for name in filter(None, args.reference_cuda.split(","))}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
