@@ -186,7 +186,7 @@ def core_library():
     return lib
 
 
-PHASES = ("prepare", "bin", "search", "scan", "readback", "write")
+PHASES = ("prepare", "bin", "count", "scan", "readback", "write")
 
 
 def phase_times(lib):
@@ -311,9 +311,7 @@ def roofline(w, n_pairs, phase_ms, step_ms):
     kernel_phases = [k for k in range(6) if PHASES[k] != "readback"]
     dominant = max(kernel_phases, key=lambda k: phase_ms[k])
     achieved = algorithmic / (phase_ms[dominant] * 1e-3) / 1e9
-    # One-pass calls emit inside the search phase; the write phase then only
-    # exists for two-pass (sorted) calls.
-    write = algorithmic / (phase_ms[5] * 1e-3) / 1e9 if phase_ms[5] > 0.01 else None
+    write = algorithmic / (phase_ms[5] * 1e-3) / 1e9 if phase_ms[5] > 0 else None
     call = algorithmic / (step_ms * 1e-3) / 1e9
     per_pair = TRAFFIC_PER_PAIR.get((w.name.split("[")[0], PHASES[dominant]))
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -56,50 +56,6 @@ constexpr int64_t kMaximumBinsPerImage = 64;
 constexpr int64_t kMaximumTotalBins = int64_t{1} << 28;
 constexpr int kRoundoffFactor = 64;
 
-// One-pass emission (unsorted calls) takes its output rows from a cursor
-// into buffers sized by this estimate; TONARI_B200_TWO_PASS=1 forces the
-// count -> scan -> write passes instead (results do not depend on it).
-bool one_pass_allowed() {
-    static const bool value = [] {
-        const char* text = std::getenv("TONARI_B200_TWO_PASS");
-        return !(text && text[0] == '1');
-    }();
-    return value;
-}
-
-// Expected pairs of one structure: N * rho * (4/3) pi rc^3 * s, rho the atom
-// density of its cell and s the mean fraction of a cutoff sphere inside the
-// cell along the non-periodic axes (1 - 3 rc / (8 w) for a slab of
-// perpendicular width w >= rc, 0.625 w / rc below), at most N * N * images;
-// halved for half lists, plus N self pairs with include_self.  Returns a
-// negative value when the cell has no volume (no density to go by).
-template <typename T>
-double expected_pairs(int64_t n, const T* cell, const uint8_t* pbc, int64_t images, double cutoff,
-                      bool half_list, bool include_self) {
-    if (n == 0) return 0.0;
-    double a[9];
-    for (int k = 0; k < 9; ++k) a[k] = static_cast<double>(cell[k]);
-    const double cross[3][3] = {
-        {a[4] * a[8] - a[5] * a[7], a[5] * a[6] - a[3] * a[8], a[3] * a[7] - a[4] * a[6]},
-        {a[7] * a[2] - a[8] * a[1], a[8] * a[0] - a[6] * a[2], a[6] * a[1] - a[7] * a[0]},
-        {a[1] * a[5] - a[2] * a[4], a[2] * a[3] - a[0] * a[5], a[0] * a[4] - a[1] * a[3]}};
-    const double volume = std::abs(a[0] * cross[0][0] + a[1] * cross[0][1] + a[2] * cross[0][2]);
-    if (!(volume > 0.0) || !std::isfinite(volume)) return -1.0;
-    double inside = 1.0;
-    for (int axis = 0; axis < 3; ++axis) {
-        if (pbc[axis]) continue;
-        const double area = std::sqrt(cross[axis][0] * cross[axis][0] + cross[axis][1] * cross[axis][1] +
-                                      cross[axis][2] * cross[axis][2]);
-        const double width = volume / area;
-        const double slab = width >= cutoff ? 1.0 - 3.0 * cutoff / (8.0 * width) : 0.625 * width / cutoff;
-        inside *= std::min(1.0, std::max(0.0, slab));
-    }
-    const double sphere = 4.0 / 3.0 * 3.14159265358979323846 * cutoff * cutoff * cutoff;
-    const double nd = static_cast<double>(n);
-    const double per_atom = std::min(nd / volume * sphere * inside, nd * static_cast<double>(images));
-    return nd * per_atom * (half_list ? 0.5 : 1.0) + (include_self ? nd : 0.0);
-}
-
 thread_local int64_t g_launches = 0;
 thread_local float g_phase_ms[6] = {0, 0, 0, 0, 0, 0};
 constexpr int kHostMarks = 12;
@@ -709,34 +665,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     const int64_t n_cell_atoms = cell_prefix.back();
     const int64_t n_brute_atoms = brute_prefix.back();
-
-    // Unsorted calls emit in one pass into buffers of an estimated capacity
-    // (the pair order is unspecified for them); a cell without volume gives
-    // no density to estimate from, and such calls take the two passes.
-    const uint32_t q = request.quantities;
-    bool one_pass = !request.sorted && q != 0 && !(q & TNR_Q_EDGE) && one_pass_allowed();
-    int64_t capacity = 0;
-    if (one_pass) {
-        double expected = 0.0;
-        int64_t nonempty = 0;
-        for (int64_t b = 0; b < batch && one_pass; ++b) {
-            if (counts[b] == 0) continue;
-            ++nonempty;
-            const int64_t images = geometry.image_begin[b + 1] - geometry.image_begin[b];
-            double e = expected_pairs<T>(counts[b], cell_t.data() + 9 * b, pbc.data() + 3 * b,
-                                         images, request.cutoff, request.half_list != 0,
-                                         request.include_self != 0);
-            if (e < 0.0) {
-                if (mode[b] != kModeBrute) one_pass = false;
-                const double nd = static_cast<double>(counts[b]);
-                e = nd * nd * static_cast<double>(images);  // every candidate
-            }
-            expected += e;
-        }
-        const double rows = 1.05 * expected + 32.0 * static_cast<double>(nonempty) + 1024.0;
-        if (!(rows < 4.0e18)) one_pass = false;
-        capacity = static_cast<int64_t>(rows);
-    }
     std::vector<int64_t> cell_bin_prefix;
     for (int32_t b : cell_structs) cell_bin_prefix.push_back(plans[b].bin_begin);
     cell_bin_prefix.push_back(total_bins);
@@ -795,7 +723,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                         stream);
         check_launch("bin scan kernel");
         // Bitmask words for the count pass -> write pass hand-off: per-bin
-        // word counts, scanned into per-bin offsets (two-pass calls only).
+        // word counts, scanned into per-bin offsets.
         SearchArgs<T> words_args{};
         words_args.plans = d_plans;
         words_args.bin_start = d_bin_start;
@@ -804,29 +732,24 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         words_args.n_cell = bin_args.n_cell;
         words_args.n_bins = total_bins;
         words_args.bin_struct = d_bin_struct;
-        if (!one_pass) {
-            auto* d_bin_words = workspace.get<unsigned long long>(total_bins);
-            d_bin_word_start = workspace.get<unsigned long long>(total_bins + 1);
-            launch_stencil_words(words_args, d_bin_words, stream);
-            check_launch("stencil words kernel");
-            launch_scan_u64(d_bin_words, total_bins, d_bin_word_start, nullptr, d_scan_workspace,
-                            d_status, stream);
-            check_launch("mask scan kernel");
-        }
+        auto* d_bin_words = workspace.get<unsigned long long>(total_bins);
+        d_bin_word_start = workspace.get<unsigned long long>(total_bins + 1);
+        launch_stencil_words(words_args, d_bin_words, stream);
+        check_launch("stencil words kernel");
+        launch_scan_u64(d_bin_words, total_bins, d_bin_word_start, nullptr, d_scan_workspace,
+                        d_status, stream);
+        check_launch("mask scan kernel");
         unsigned long long packed_total = 0, mask_words = 0;
         check_cuda(cudaMemcpyAsync(pinned_read, d_bin_start + total_bins, sizeof(packed_total),
                                    cudaMemcpyDeviceToHost, stream), "read ghost total");
-        if (!one_pass) {
-            check_cuda(cudaMemcpyAsync(pinned_read + 8, d_bin_word_start + total_bins,
-                                       sizeof(mask_words), cudaMemcpyDeviceToHost, stream),
-                       "read mask words");
-        }
+        check_cuda(cudaMemcpyAsync(pinned_read + 8, d_bin_word_start + total_bins, sizeof(mask_words),
+                                   cudaMemcpyDeviceToHost, stream), "read mask words");
         check_cuda(cudaStreamSynchronize(stream), "ghost total");
         std::memcpy(&packed_total, pinned_read, sizeof(packed_total));
-        if (!one_pass) std::memcpy(&mask_words, pinned_read + 8, sizeof(mask_words));
+        std::memcpy(&mask_words, pinned_read + 8, sizeof(mask_words));
         timer.host(5);  // ghost and mask totals read back
         require_search(mask_words < (1ull << 32), "cell-list candidate bitmask exceeds uint32 indexing");
-        if (!one_pass) d_mask_words = workspace.get<uint32_t>(mask_words);
+        d_mask_words = workspace.get<uint32_t>(mask_words);
         const int64_t ghosts = static_cast<int64_t>(packed_total & 0xffffffffull);
         const int64_t sources = static_cast<int64_t>(packed_total >> 32);
         require_search(sources == n_cell_atoms && ghosts >= sources &&
@@ -851,33 +774,10 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     timer.mark(2);
 
-    // While the search runs: the exact geometry (the reference's long-double
-    // arithmetic) must give the same T duals and image ranges as the device,
-    // else the call is repeated on the host path.  Its input errors are
-    // raised by that repeat, in the reference's order.
-    auto verify_speculation = [&]() {
-        if (!speculate) return;
-        const PeriodicGeometry exact =
-            build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
-        for (int64_t b = 0; b < batch; ++b) {
-            for (int a = 0; a < 3; ++a) {
-                if (exact.repeats[3 * b + a] != geometry.repeats[3 * b + a]) throw SpeculationFailed{};
-            }
-            if (exact.image_begin[b + 1] != geometry.image_begin[b + 1]) throw SpeculationFailed{};
-        }
-        // The duals may differ in their last bits (the device rounds in
-        // double); what the search used of them is the wraps, which the
-        // device now recomputes with the exact duals (status word 2).
-        T* exact_duals = reinterpret_cast<T*>(pinned_prepare);
-        for (int64_t k = 0; k < 9 * batch; ++k) exact_duals[k] = static_cast<T>(exact.duals[k]);
-        T* d_exact_duals = workspace.get<T>(9 * batch);
-        check_cuda(cudaMemcpyAsync(d_exact_duals, exact_duals, 9 * batch * sizeof(T),
-                                   cudaMemcpyHostToDevice, stream), "upload exact duals");
-        launch_verify_wraps<T>(static_cast<const T*>(request.positions), n_atoms, d_atom_struct,
-                               d_exact_duals, d_wraps, d_status + 2, stream);
-        check_launch("wrap check kernel");
-    };
-
+    // ---- count pass -> scan -> exact E -------------------------------------
+    auto* d_counts = workspace.get<uint32_t>(n_atoms);
+    auto* d_pair_start = workspace.get<int64_t>(n_atoms + 1);
+    check_cuda(cudaMemsetAsync(d_counts, 0, n_atoms * sizeof(uint32_t), stream), "memset counts");
     SearchArgs<T> search{};
     search.positions = static_cast<const T*>(request.positions);
     search.atom_struct = d_atom_struct;
@@ -905,90 +805,12 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.brute_structs = reinterpret_cast<const int32_t*>(second_device + off_brute_structs);
     search.n_brute = static_cast<int32_t>(brute_structs.size());
     search.n_brute_atoms = n_brute_atoms;
+    search.counts = d_counts;
+    search.pair_start = d_pair_start;
     search.index_offset = request.index_offset;
     search.status = d_status;
     search.half_list = request.half_list ? 1 : 0;
     search.include_self = request.include_self ? 1 : 0;
-
-    if (one_pass) {
-        // ---- one pass: search and emission, rows from the cursor --------
-        auto* d_cursor = workspace.get<unsigned long long>(1);
-        auto allocate_outputs = [&](int64_t rows) {
-            const size_t e = static_cast<size_t>(std::max<int64_t>(rows, 1));
-            if (q & TNR_Q_I) result.i = workspace.output<int64_t>(e);
-            if (q & TNR_Q_J) result.j = workspace.output<int64_t>(e);
-            if (q & TNR_Q_P) result.P = workspace.output<int64_t>(2 * e);
-            if (q & TNR_Q_S) result.S = workspace.output<int32_t>(3 * e);
-            if (q & TNR_Q_d) result.d = workspace.output<T>(e);
-            if (q & TNR_Q_D) result.D = workspace.output<T>(3 * e);
-            search.out_i = result.i;
-            search.out_j = result.j;
-            search.out_P = result.P;
-            search.out_S = result.S;
-            search.out_d = static_cast<T*>(result.d);
-            search.out_D = static_cast<T*>(result.D);
-            search.cursor = d_cursor;
-            search.capacity = rows;
-            check_cuda(cudaMemsetAsync(d_cursor, 0, sizeof(unsigned long long), stream),
-                       "memset cursor");
-        };
-        auto launch_one_pass = [&]() {
-            if (n_cell_atoms) {
-                launch_cell_fused(search, stream);
-                check_launch("cell search kernel");
-            }
-            if (n_brute_atoms) {
-                launch_brute_fused(search, stream);
-                check_launch("brute search kernel");
-            }
-        };
-        allocate_outputs(capacity);
-        launch_one_pass();
-        timer.mark(3);
-        timer.host(6);  // search launched
-        verify_speculation();
-        timer.mark(4);
-        check_cuda(cudaMemcpyAsync(pinned_read, d_cursor, sizeof(unsigned long long),
-                                   cudaMemcpyDeviceToHost, stream), "read pair total");
-        check_cuda(cudaMemcpyAsync(pinned_read + sizeof(int64_t), d_status, 3 * sizeof(uint32_t),
-                                   cudaMemcpyDeviceToHost, stream), "read status");
-        check_cuda(cudaStreamSynchronize(stream), "pair total");
-        unsigned long long rows = 0;
-        uint32_t status = 0, wraps_differ = 0;
-        std::memcpy(&rows, pinned_read, sizeof(rows));
-        std::memcpy(&status, pinned_read + sizeof(int64_t), sizeof(status));
-        std::memcpy(&wraps_differ, pinned_read + sizeof(int64_t) + 2 * sizeof(uint32_t),
-                    sizeof(wraps_differ));
-        if (speculate && wraps_differ) throw SpeculationFailed{};
-        timer.host(7);  // pair total read back
-        check_status(status);
-        require_search(rows < (1ull << 62), "neighbor-list output exceeds the int64 range");
-        const int64_t n_pairs = static_cast<int64_t>(rows);
-        timer.mark(5);
-        if (n_pairs > capacity) {
-            // The estimate fell short: the pass is repeated into buffers of
-            // the exact size, which the first pass has counted.
-            workspace.release_outputs();
-            allocate_outputs(n_pairs);
-            launch_one_pass();
-        }
-        result.n_pairs = n_pairs;
-        if (n_pairs == 0) {
-            workspace.release_outputs();
-            result = tnr_result{};
-        }
-        timer.mark(6);
-        timer.host(8);  // output complete or repeat launched
-        timer.finish();
-        return;
-    }
-
-    // ---- count pass -> scan -> exact E -------------------------------------
-    auto* d_counts = workspace.get<uint32_t>(n_atoms);
-    auto* d_pair_start = workspace.get<int64_t>(n_atoms + 1);
-    check_cuda(cudaMemsetAsync(d_counts, 0, n_atoms * sizeof(uint32_t), stream), "memset counts");
-    search.counts = d_counts;
-    search.pair_start = d_pair_start;
     if (n_cell_atoms) {
         launch_cell_search(search, false, stream);
         check_launch("cell count kernel");
@@ -999,7 +821,31 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     timer.mark(3);
     timer.host(6);  // count pass launched
-    verify_speculation();
+    if (speculate) {
+        // While the search runs: the exact geometry (the reference's long-
+        // double arithmetic) must give the same T duals and image ranges as
+        // the device, else the call is repeated on the host path.  Its input
+        // errors are raised by that repeat, in the reference's order.
+        const PeriodicGeometry exact =
+            build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
+        for (int64_t b = 0; b < batch; ++b) {
+            for (int a = 0; a < 3; ++a) {
+                if (exact.repeats[3 * b + a] != geometry.repeats[3 * b + a]) throw SpeculationFailed{};
+            }
+            if (exact.image_begin[b + 1] != geometry.image_begin[b + 1]) throw SpeculationFailed{};
+        }
+        // The duals may differ in their last bits (the device rounds in
+        // double); what the search used of them is the wraps, which the
+        // device now recomputes with the exact duals (status word 2).
+        T* exact_duals = reinterpret_cast<T*>(pinned_prepare);
+        for (int64_t k = 0; k < 9 * batch; ++k) exact_duals[k] = static_cast<T>(exact.duals[k]);
+        T* d_exact_duals = workspace.get<T>(9 * batch);
+        check_cuda(cudaMemcpyAsync(d_exact_duals, exact_duals, 9 * batch * sizeof(T),
+                                   cudaMemcpyHostToDevice, stream), "upload exact duals");
+        launch_verify_wraps<T>(static_cast<const T*>(request.positions), n_atoms, d_atom_struct,
+                               d_exact_duals, d_wraps, d_status + 2, stream);
+        check_launch("wrap check kernel");
+    }
     launch_scan_counts(d_counts, n_atoms, d_pair_start, d_scan_workspace, d_status, stream);
     check_launch("pair scan kernel");
     timer.mark(4);
@@ -1021,6 +867,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     // ---- exact-size outputs and the write pass -----------------------------
     result.n_pairs = n_pairs;
     if (n_pairs == 0) return;
+    const uint32_t q = request.quantities;
     const size_t e = static_cast<size_t>(n_pairs);
     if (q & TNR_Q_I) result.i = workspace.output<int64_t>(e);
     if (q & TNR_Q_J) result.j = workspace.output<int64_t>(e);

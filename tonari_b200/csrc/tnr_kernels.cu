@@ -475,14 +475,6 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
 // search: count pass and write pass
 // ---------------------------------------------------------------------------
 
-// First of `n` output rows taken from the call's row cursor by lane 0 and
-// handed to the whole warp (warp-uniform call).
-__device__ __forceinline__ int64_t take_rows(unsigned long long* cursor, int n, int lane) {
-    unsigned long long first = 0;
-    if (lane == 0) first = atomicAdd(cursor, static_cast<unsigned long long>(n));
-    return static_cast<int64_t>(__shfl_sync(kFullMask, first, 0));
-}
-
 // Writes one accepted pair at output row `o`.
 template <typename T>
 __device__ __forceinline__ void emit_pair(const SearchArgs<T>& a, int64_t o, int64_t source,
@@ -750,96 +742,6 @@ __device__ __forceinline__ uint32_t push_key(uint32_t bits, uint32_t source_key_
     return __funnelshift_l(source_key_plus_one - candidate_key, bits, 1);
 }
 
-// One tile of the stencil walk: this lane's candidate `cand` (ghost `slot`)
-// against the staged block of sources (sx/sy/sz wrapped positions, skey keys,
-// `padded` entries of which `block` are real).  Returns bit r set when the
-// pair (source r, candidate) is kept -- except the zero-shift self pair,
-// which the callers settle per include_self.  Candidates in the band shell
-// between the inner and search radius, and half-list images of a source
-// itself, are decided exactly by the candidate's lane (the rare path).
-template <typename T, bool Half>
-__device__ __forceinline__ uint32_t tile_keep_bits(
-    const SearchArgs<T>& args, const StructurePlan<T>& plan, const vec4_t<T>& cand, int32_t slot,
-    const T* __restrict__ sx, const T* __restrict__ sy, const T* __restrict__ sz,
-    const uint32_t* __restrict__ skey, int padded, int block, uint32_t valid_mask,
-    unsigned long long inner_pair, unsigned long long search_pair, T inner2, T search2,
-    bool self_images) {
-    const uint32_t key = static_cast<uint32_t>(lane_to_index(cand.w));
-    uint32_t key_signs = 0;  // half lists: bit r = key(s_r) + 1 < key(c)
-    uint32_t inner_signs = 0, search_signs = 0;
-    if constexpr (std::is_same<T, float>::value) {
-        const unsigned long long cx = pack2(cand.x, cand.x);
-        const unsigned long long cy = pack2(cand.y, cand.y);
-        const unsigned long long cz = pack2(cand.z, cand.z);
-        for (int r0 = 0; r0 < padded; r0 += 4) {
-            const ulonglong2 qx = *reinterpret_cast<const ulonglong2*>(&sx[r0]);
-            const ulonglong2 qy = *reinterpret_cast<const ulonglong2*>(&sy[r0]);
-            const ulonglong2 qz = *reinterpret_cast<const ulonglong2*>(&sz[r0]);
-            const unsigned long long d01 = distance2_pair(cx, cy, cz, qx.x, qy.x, qz.x);
-            const unsigned long long d23 = distance2_pair(cx, cy, cz, qx.y, qy.y, qz.y);
-            inner_signs = push_signs2(push_signs2(inner_signs, sub2(d01, inner_pair)),
-                                      sub2(d23, inner_pair));
-            search_signs = push_signs2(push_signs2(search_signs, sub2(d01, search_pair)),
-                                       sub2(d23, search_pair));
-            if constexpr (Half) {
-                const uint4 k = *reinterpret_cast<const uint4*>(&skey[r0]);
-                key_signs = push_key(push_key(push_key(push_key(key_signs, k.x, key), k.y, key),
-                                              k.z, key), k.w, key);
-            }
-        }
-    } else {
-        for (int r = 0; r < padded; ++r) {
-            const T d2 = screen_distance2(cand.x, cand.y, cand.z, sx[r], sy[r], sz[r]);
-            inner_signs = push_sign(inner_signs, d2 - inner2);
-            search_signs = push_sign(search_signs, d2 - search2);
-            if constexpr (Half) key_signs = push_key(key_signs, skey[r], key);
-        }
-    }
-    // Bit r: d2 to source r below the inner / search radius.
-    const uint32_t inside = __brev(inner_signs) >> (32 - padded);
-    const uint32_t near = __brev(search_signs) >> (32 - padded);
-    uint32_t keep_keys = valid_mask, band_keys = valid_mask;
-    if constexpr (Half) {
-        keep_keys = band_keys = (__brev(key_signs) >> (32 - padded)) & valid_mask;
-        // key(c) == key(s) + 1: an image of source s itself, only
-        // possible where a lattice translation is shorter than the
-        // search radius; its shift decides it in the rare path.
-        if (self_images && (key & 1u) == 0u && key != 0u) {
-            for (int r = 0; r < block; ++r) {
-                if (skey[r] == key) band_keys |= 1u << r;
-            }
-        }
-    }
-    uint32_t keep_bits = inside & keep_keys;
-    uint32_t rare = near & band_keys & ~keep_bits;
-    if (__any_sync(kFullMask, rare != 0u) && rare != 0u) {
-        // Rare: band shell, or a half-list periodic image of the
-        // source itself; decided exactly by the candidate's lane.
-        const int4 meta = args.ghost_meta[slot];  // .w: the candidate's atom
-        do {
-            const int r = __ffs(rare) - 1;
-            rare &= rare - 1u;
-            const uint32_t key_r = skey[r];
-            const int32_t source = static_cast<int32_t>(Half ? (key_r - 2u) >> 1 : key_r);
-            const long long shift[3] = {
-                meta.x + static_cast<long long>(args.wraps[3 * source]),
-                meta.y + static_cast<long long>(args.wraps[3 * source + 1]),
-                meta.z + static_cast<long long>(args.wraps[3 * source + 2])};
-            bool keep = true;
-            if (Half && meta.w == source) keep = canonical_shift(shift);
-            if (keep && !((inside >> r) & 1u)) {
-                const T* pt = args.positions + 3 * static_cast<int64_t>(meta.w);
-                const T vx = exact_component(pt[0], args.positions[3 * source], shift, plan.cell, 0);
-                const T vy = exact_component(pt[1], args.positions[3 * source + 1], shift, plan.cell, 1);
-                const T vz = exact_component(pt[2], args.positions[3 * source + 2], shift, plan.cell, 2);
-                keep = exact_norm2(vx, vy, vz) < plan.cutoff_squared;
-            }
-            if (keep) keep_bits |= 1u << r;
-        } while (rare != 0u);
-    }
-    return keep_bits;
-}
-
 template <typename T, bool Half>
 __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
@@ -949,10 +851,80 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 const V cand = next;
                 const int32_t slot = next_slot;
                 if (w + 1 < words) load_candidate(w + 1, next, next_slot);
-                const uint32_t keep_bits = tile_keep_bits<T, Half>(
-                    args, plan, cand, slot, source_x[warp], source_y[warp], source_z[warp],
-                    source_key[warp], padded, block, valid_mask, inner_pair, search_pair, inner2,
-                    search2, self_images);
+                const uint32_t key = static_cast<uint32_t>(lane_to_index(cand.w));
+                uint32_t key_signs = 0;  // half lists: bit r = key(s_r) + 1 < key(c)
+                uint32_t inner_signs = 0, search_signs = 0;
+                if constexpr (std::is_same<T, float>::value) {
+                    const unsigned long long cx = pack2(cand.x, cand.x);
+                    const unsigned long long cy = pack2(cand.y, cand.y);
+                    const unsigned long long cz = pack2(cand.z, cand.z);
+                    for (int r0 = 0; r0 < padded; r0 += 4) {
+                        const ulonglong2 sx = *reinterpret_cast<const ulonglong2*>(&source_x[warp][r0]);
+                        const ulonglong2 sy = *reinterpret_cast<const ulonglong2*>(&source_y[warp][r0]);
+                        const ulonglong2 sz = *reinterpret_cast<const ulonglong2*>(&source_z[warp][r0]);
+                        const unsigned long long d01 = distance2_pair(cx, cy, cz, sx.x, sy.x, sz.x);
+                        const unsigned long long d23 = distance2_pair(cx, cy, cz, sx.y, sy.y, sz.y);
+                        inner_signs = push_signs2(push_signs2(inner_signs, sub2(d01, inner_pair)),
+                                                  sub2(d23, inner_pair));
+                        search_signs = push_signs2(push_signs2(search_signs, sub2(d01, search_pair)),
+                                                   sub2(d23, search_pair));
+                        if constexpr (Half) {
+                            const uint4 k = *reinterpret_cast<const uint4*>(&source_key[warp][r0]);
+                            key_signs = push_key(push_key(push_key(push_key(key_signs, k.x, key), k.y, key),
+                                                          k.z, key), k.w, key);
+                        }
+                    }
+                } else {
+                    for (int r = 0; r < padded; ++r) {
+                        const T d2 = screen_distance2(cand.x, cand.y, cand.z, source_x[warp][r],
+                                                      source_y[warp][r], source_z[warp][r]);
+                        inner_signs = push_sign(inner_signs, d2 - inner2);
+                        search_signs = push_sign(search_signs, d2 - search2);
+                        if constexpr (Half) key_signs = push_key(key_signs, source_key[warp][r], key);
+                    }
+                }
+                // Bit r: d2 to source r below the inner / search radius.
+                const uint32_t inside = __brev(inner_signs) >> (32 - padded);
+                const uint32_t near = __brev(search_signs) >> (32 - padded);
+                uint32_t keep_keys = valid_mask, band_keys = valid_mask;
+                if constexpr (Half) {
+                    keep_keys = band_keys = (__brev(key_signs) >> (32 - padded)) & valid_mask;
+                    // key(c) == key(s) + 1: an image of source s itself, only
+                    // possible where a lattice translation is shorter than the
+                    // search radius; its shift decides it in the rare path.
+                    if (self_images && (key & 1u) == 0u && key != 0u) {
+                        for (int r = 0; r < block; ++r) {
+                            if (source_key[warp][r] == key) band_keys |= 1u << r;
+                        }
+                    }
+                }
+                uint32_t keep_bits = inside & keep_keys;
+                uint32_t rare = near & band_keys & ~keep_bits;
+                if (__any_sync(kFullMask, rare != 0u) && rare != 0u) {
+                    // Rare: band shell, or a half-list periodic image of the
+                    // source itself; decided exactly by the candidate's lane.
+                    const int4 meta = args.ghost_meta[slot];  // .w: the candidate's atom
+                    do {
+                        const int r = __ffs(rare) - 1;
+                        rare &= rare - 1u;
+                        const uint32_t key_r = source_key[warp][r];
+                        const int32_t source = static_cast<int32_t>(Half ? (key_r - 2u) >> 1 : key_r);
+                        const long long shift[3] = {
+                            meta.x + static_cast<long long>(args.wraps[3 * source]),
+                            meta.y + static_cast<long long>(args.wraps[3 * source + 1]),
+                            meta.z + static_cast<long long>(args.wraps[3 * source + 2])};
+                        bool keep = true;
+                        if (Half && meta.w == source) keep = canonical_shift(shift);
+                        if (keep && !((inside >> r) & 1u)) {
+                            const T* pt = args.positions + 3 * static_cast<int64_t>(meta.w);
+                            const T vx = exact_component(pt[0], args.positions[3 * source], shift, plan.cell, 0);
+                            const T vy = exact_component(pt[1], args.positions[3 * source + 1], shift, plan.cell, 1);
+                            const T vz = exact_component(pt[2], args.positions[3 * source + 2], shift, plan.cell, 2);
+                            keep = exact_norm2(vx, vy, vz) < plan.cutoff_squared;
+                        }
+                        if (keep) keep_bits |= 1u << r;
+                    } while (rare != 0u);
+                }
                 // Transpose the warp's 32 x 32 bit matrix: afterwards lane r
                 // holds source r's word (bit c = candidate lane c accepted).
                 const uint32_t my_word_bits = transpose_bits32(keep_bits, lane);
@@ -1457,267 +1429,6 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
 }
 
 
-// One-pass cell-list search and emission (unsorted calls).  The warp serves
-// one bin as the count pass does -- lanes = 32 stencil candidates per tile,
-// the bin's sources (32 at a time) staged in shared memory -- and appends the
-// kept (candidate slot, source) entries of every tile to its queue in shared
-// memory.  Once the queue holds kFusedFlush entries, and at the end of each
-// block of sources, the warp takes that many output rows from the call's row
-// cursor (one atomic) and writes them: each lane loads its entry's ghost
-// records, evaluates the public displacement with the bin's cell (held in
-// registers) and stores its rows.  Rows at or beyond args.capacity are
-// counted but not written; the cursor's final value is the pair count.
-#ifndef TNR_FUSED_THREADS
-#define TNR_FUSED_THREADS 128
-#endif
-#ifndef TNR_FUSED_FLUSH
-#define TNR_FUSED_FLUSH 256
-#endif
-#ifndef TNR_FUSED_MIN_BLOCKS
-#define TNR_FUSED_MIN_BLOCKS 1
-#endif
-constexpr int kFusedThreads = TNR_FUSED_THREADS;
-constexpr int kFusedWarps = kFusedThreads / 32;
-constexpr int kFusedFlush = TNR_FUSED_FLUSH;
-constexpr int kFusedQueue = kFusedFlush + 32 * 32;  // + one tile's worst case
-
-template <typename T>
-struct FusedShared {
-    StencilRows rows;
-    alignas(16) T sx[32];      // wrapped source positions (screening)
-    alignas(16) T sy[32];
-    alignas(16) T sz[32];
-    alignas(16) uint32_t skey[32];
-    T px[32];                  // original source positions (emission)
-    T py[32];
-    T pz[32];
-    int32_t wx[32];            // source wraps
-    int32_t wy[32];
-    int32_t wz[32];
-    int32_t atom[32];
-    int32_t q_slot[kFusedQueue];
-    uint8_t q_r[kFusedQueue];
-};
-
-template <typename T, int Q>
-__device__ __forceinline__ void fused_flush(const SearchArgs<T>& args, FusedShared<T>& sh,
-                                            int32_t queued, const T (&cell)[9], int lane,
-                                            bool need_shift, bool need_vector) {
-    using V = vec4_t<T>;
-    __syncwarp();
-    const int64_t base = take_rows(args.cursor, queued, lane);
-    for (int32_t e0 = 0; e0 < queued; e0 += 64) {
-        int4 meta[2];
-        V pt[2];
-        int32_t r[2];
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-            const int32_t e = e0 + 32 * m + lane;
-            r[m] = -1;
-            if (e < queued) {
-                const int32_t slot = sh.q_slot[e];
-                r[m] = sh.q_r[e];
-                meta[m] = args.ghost_meta[slot];
-                if (need_vector) pt[m] = reinterpret_cast<const V*>(args.ghost_orig)[slot];
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-            const int64_t o = base + e0 + 32 * m + lane;
-            if (r[m] < 0 || o >= args.capacity) continue;
-            const int32_t q = r[m];
-            int32_t shift[3] = {0, 0, 0};
-            T vec[3] = {T(0), T(0), T(0)};
-            if (need_shift) {
-                // Cell-list shifts fit int32 by construction of the plan.
-                shift[0] = meta[m].x + sh.wx[q];
-                shift[1] = meta[m].y + sh.wy[q];
-                shift[2] = meta[m].z + sh.wz[q];
-            }
-            if (need_vector) {
-                const T s0 = static_cast<T>(shift[0]);
-                const T s1 = static_cast<T>(shift[1]);
-                const T s2 = static_cast<T>(shift[2]);
-                vec[0] = add_rn(add_rn(add_rn(sub_rn(pt[m].x, sh.px[q]), mul_rn(s0, cell[0])),
-                                       mul_rn(s1, cell[3])), mul_rn(s2, cell[6]));
-                vec[1] = add_rn(add_rn(add_rn(sub_rn(pt[m].y, sh.py[q]), mul_rn(s0, cell[1])),
-                                       mul_rn(s1, cell[4])), mul_rn(s2, cell[7]));
-                vec[2] = add_rn(add_rn(add_rn(sub_rn(pt[m].z, sh.pz[q]), mul_rn(s0, cell[2])),
-                                       mul_rn(s1, cell[5])), mul_rn(s2, cell[8]));
-            }
-            const int64_t si = static_cast<int64_t>(sh.atom[q]) + args.index_offset;
-            const int64_t ti = static_cast<int64_t>(meta[m].w) + args.index_offset;
-            if (wants<Q>(args.out_i, kQ_I)) args.out_i[o] = si;
-            if (wants<Q>(args.out_j, kQ_J)) args.out_j[o] = ti;
-            if (wants<Q>(args.out_P, kQ_P)) {
-                reinterpret_cast<longlong2*>(args.out_P)[o] = make_longlong2(si, ti);
-            }
-            if (wants<Q>(args.out_S, kQ_S)) {
-                int32_t* row = args.out_S + 3 * o;
-                row[0] = shift[0];
-                row[1] = shift[1];
-                row[2] = shift[2];
-            }
-            if (wants<Q>(args.out_d, kQ_d)) args.out_d[o] = pair_distance(vec[0], vec[1], vec[2]);
-            if (wants<Q>(args.out_D, kQ_D)) {
-                T* row = args.out_D + 3 * o;
-                row[0] = vec[0];
-                row[1] = vec[1];
-                row[2] = vec[2];
-            }
-        }
-    }
-    __syncwarp();
-}
-
-template <typename T, bool Half, int Q>
-__global__ void __launch_bounds__(kFusedThreads, TNR_FUSED_MIN_BLOCKS) cell_fused_kernel(SearchArgs<T> args) {
-    using V = vec4_t<T>;
-    __shared__ FusedShared<T> shared[kFusedWarps];
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    FusedShared<T>& sh = shared[warp];
-    const bool need_vector = wants<Q>(args.out_d, kQ_d) || wants<Q>(args.out_D, kQ_D);
-    const bool need_shift = wants<Q>(args.out_S, kQ_S) || need_vector;
-    const int64_t stride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-         base < args.n_bins; base += 32 * stride) {
-      // As in the count pass: probe 32 of the warp's strided bins at once and
-      // visit those with sources.
-      const int64_t my_bin = base + lane * stride;
-      uint32_t my_first = 0, my_count = 0;
-      if (my_bin < args.n_bins) {
-          my_first = static_cast<uint32_t>(args.bin_start[my_bin] >> 32);
-          my_count = static_cast<uint32_t>(args.bin_start[my_bin + 1] >> 32) - my_first;
-      }
-      unsigned pending = __ballot_sync(kFullMask, my_count != 0u);
-      while (pending != 0u) {
-        const int chosen = __ffs(pending) - 1;
-        pending &= pending - 1u;
-        const int64_t bin = base + chosen * stride;
-        const uint32_t first_source = __shfl_sync(kFullMask, my_first, chosen);
-        const uint32_t n_sources = __shfl_sync(kFullMask, my_count, chosen);
-        const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
-        int32_t bx, by, bz;
-        bin_coordinates(plan, bin, bx, by, bz);
-        StencilRows& rows = sh.rows;
-        const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz, &rows, lane);
-        const int32_t words = (total + 31) >> 5;
-        const T search2 = plan.search_squared;
-        const T inner2 = plan.inner_squared;
-        const bool self_images = plan.self_images != 0;
-        T cell[9];
-#pragma unroll
-        for (int c = 0; c < 9; ++c) cell[c] = need_vector ? plan.cell[c] : T(0);
-        unsigned long long inner_pair = 0, search_pair = 0;
-        if constexpr (std::is_same<T, float>::value) {
-            inner_pair = pack2(inner2, inner2);
-            search_pair = pack2(search2, search2);
-        }
-
-        for (uint32_t block_base = 0; block_base < n_sources; block_base += 32) {
-            const int block = static_cast<int>(min(32u, n_sources - block_base));
-            const int padded = (block + 3) & ~3;
-            const uint32_t valid_mask = block == 32 ? kFullMask : (1u << block) - 1u;
-            int32_t self_k = -1;  // candidate index of my source's zero image
-            __syncwarp();
-            if (lane < block) {
-                const int32_t source = args.source_list[first_source + block_base + lane];
-                const V q = reinterpret_cast<const V*>(args.wrapped)[source];
-                sh.sx[lane] = q.x;
-                sh.sy[lane] = q.y;
-                sh.sz[lane] = q.z;
-                sh.skey[lane] = Half ? 2u * static_cast<uint32_t>(source) + 2u
-                                     : static_cast<uint32_t>(source);
-                sh.atom[lane] = source;
-                sh.wx[lane] = args.wraps[3 * source];
-                sh.wy[lane] = args.wraps[3 * source + 1];
-                sh.wz[lane] = args.wraps[3 * source + 2];
-                if (need_vector) {
-                    sh.px[lane] = args.positions[3 * static_cast<int64_t>(source)];
-                    sh.py[lane] = args.positions[3 * static_cast<int64_t>(source) + 1];
-                    sh.pz[lane] = args.positions[3 * static_cast<int64_t>(source) + 2];
-                }
-                const int32_t self = args.self_slot[source];
-#pragma unroll
-                for (int r = 0; r < 9; ++r) {
-                    const int32_t begin_r = rows.prefix[r] + rows.delta[r];
-                    const int32_t length_r = rows.prefix[r + 1] - rows.prefix[r];
-                    if (self >= begin_r && self < begin_r + length_r) {
-                        self_k = rows.prefix[r] + (self - begin_r);
-                    }
-                }
-            } else if (lane < padded) {
-                sh.sx[lane] = sh.sy[lane] = sh.sz[lane] = static_cast<T>(NAN);
-                sh.skey[lane] = 0u;
-            }
-            __syncwarp();
-            int32_t queued = 0;
-            int32_t row = 0;
-            int32_t row_end = rows.prefix[1];
-            auto load_candidate = [&](int32_t w, V& record, int32_t& slot) {
-                const int32_t k = 32 * w + lane;
-                if (k < total) {
-                    while (k >= row_end) row_end = rows.prefix[++row + 1];
-                    slot = k + rows.delta[row];
-                    record = reinterpret_cast<const V*>(args.ghost_pos)[slot];
-                } else {
-                    slot = -1;
-                    record.x = static_cast<T>(INFINITY);
-                    record.y = T(0);
-                    record.z = T(0);
-                    record.w = index_to_lane(0, T(0));
-                }
-            };
-            V next;
-            int32_t next_slot;
-            load_candidate(0, next, next_slot);
-            for (int32_t w = 0; w < words; ++w) {
-                const V cand = next;
-                const int32_t slot = next_slot;
-                if (w + 1 < words) load_candidate(w + 1, next, next_slot);
-                uint32_t keep_bits = tile_keep_bits<T, Half>(
-                    args, plan, cand, slot, sh.sx, sh.sy, sh.sz, sh.skey, padded, block,
-                    valid_mask, inner_pair, search_pair, inner2, search2, self_images);
-                // The zero-shift self pair of source r is candidate self_k of
-                // its stencil: kept only with include_self.
-                unsigned fix = __ballot_sync(kFullMask, lane < block && (self_k >> 5) == w);
-                while (fix != 0u) {
-                    const int r = __ffs(fix) - 1;
-                    fix &= fix - 1u;
-                    const int owner = __shfl_sync(kFullMask, self_k & 31, r);
-                    if (lane == owner) {
-                        keep_bits = args.include_self ? (keep_bits | (1u << r))
-                                                      : (keep_bits & ~(1u << r));
-                    }
-                }
-                if (!__any_sync(kFullMask, keep_bits != 0u)) continue;
-                const int32_t mine = __popc(keep_bits);
-                int32_t inclusive = mine;
-#pragma unroll
-                for (int offset = 1; offset < 32; offset <<= 1) {
-                    const int32_t other = __shfl_up_sync(kFullMask, inclusive, offset);
-                    if (lane >= offset) inclusive += other;
-                }
-                int32_t at = queued + inclusive - mine;
-                for (uint32_t bits = keep_bits; bits != 0u; bits &= bits - 1u) {
-                    sh.q_slot[at] = slot;
-                    sh.q_r[at] = static_cast<uint8_t>(__ffs(bits) - 1);
-                    ++at;
-                }
-                queued += __shfl_sync(kFullMask, inclusive, 31);
-                if (queued >= kFusedFlush) {
-                    fused_flush<T, Q>(args, sh, queued, cell, lane, need_shift, need_vector);
-                    queued = 0;
-                }
-            }
-            if (queued > 0) fused_flush<T, Q>(args, sh, queued, cell, lane, need_shift, need_vector);
-        }
-      }
-    }
-}
-
-
 // Brute force: one warp per source atom of a brute-force structure (grid-
 // stride over those atoms); lanes stride over the N x I (target, image)
 // candidates, target fastest so that consecutive lanes read consecutive
@@ -1762,11 +1473,8 @@ __device__ __forceinline__ BruteCandidate<T> brute_evaluate(const SearchArgs<T>&
     return out;
 }
 
-// Mode 0: count pass; 1: write pass at pair_start; 2: one pass, rows taken
-// from args.cursor 32 at a time (unsorted calls).
-template <typename T, int Mode>
+template <typename T, bool Write>
 __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs<T> args) {
-    constexpr bool Write = Mode != 0;
     __shared__ int2 queue[kSearchWarps][64];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1778,8 +1486,8 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
         const StructurePlan<T>& plan = args.plans[args.brute_structs[c]];
         const int64_t source = plan.atom_begin + (work - args.brute_prefix[c]);
         const int64_t order = args.source_order ? args.n_sources + work : source;
-        if constexpr (Mode == 1) {
-            if (args.counts[order] == 0) continue;
+            if constexpr (Write) {
+                if (args.counts[order] == 0) continue;
         }
         const T ps[3] = {args.positions[3 * source], args.positions[3 * source + 1],
                          args.positions[3 * source + 2]};
@@ -1794,7 +1502,7 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
         uint32_t count = 0;
         int64_t out_row = 0;
         int32_t queued = 0;
-        if constexpr (Mode == 1) out_row = args.pair_start[order];
+        if constexpr (Write) out_row = args.pair_start[order];
         // Warp-uniform trip count: ceil(n * images / 32) iterations.
         const int64_t trips = (static_cast<int64_t>(n) * images + 31) / 32;
         for (int64_t trip = 0; trip < trips; ++trip) {
@@ -1803,7 +1511,7 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
                 const BruteCandidate<T> cand =
                     brute_evaluate(args, plan, source, plan.atom_begin + t, image, ps, ws);
                 accept = cand.accept;
-                if (Mode != 1 && accept) {
+                if (!Write && accept) {
                     if (cand.shift[0] < INT_MIN || cand.shift[0] > INT_MAX ||
                         cand.shift[1] < INT_MIN || cand.shift[1] > INT_MAX ||
                         cand.shift[2] < INT_MIN || cand.shift[2] > INT_MAX) {
@@ -1819,14 +1527,11 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
                     queued += __popc(ballot);
                     if (queued >= 32) {
                         __syncwarp();
-                        if constexpr (Mode == 2) out_row = take_rows(args.cursor, 32, lane);
                         const int2 item = q[lane];
                         const BruteCandidate<T> cand = brute_evaluate(
                             args, plan, source, plan.atom_begin + item.x, item.y, ps, ws);
-                        if (Mode != 2 || out_row + lane < args.capacity) {
-                            emit_pair(args, out_row + lane, source, plan.atom_begin + item.x,
-                                      cand.shift, cand.vec);
-                        }
+                        emit_pair(args, out_row + lane, source, plan.atom_begin + item.x,
+                                  cand.shift, cand.vec);
                         __syncwarp();
                         if (lane < queued - 32) q[lane] = q[32 + lane];
                         __syncwarp();
@@ -1846,8 +1551,7 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
         }
         if constexpr (Write) {
             __syncwarp();
-            if (Mode == 2 && queued > 0) out_row = take_rows(args.cursor, queued, lane);
-            if (lane < queued && (Mode != 2 || out_row + lane < args.capacity)) {
+            if (lane < queued) {
                 const int2 item = queue[warp][lane];
                 const BruteCandidate<T> cand = brute_evaluate(
                     args, plan, source, plan.atom_begin + item.x, item.y, ps, ws);
@@ -2140,54 +1844,20 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
 }
 
 template <typename T>
-void launch_cell_fused(const SearchArgs<T>& args, cudaStream_t stream) {
-    if (args.n_sources == 0 || args.n_bins == 0) return;
-    const int64_t needed = blocks_for(args.n_bins, kFusedWarps);
-    const int q = (args.out_i ? kQ_I : 0) | (args.out_j ? kQ_J : 0) | (args.out_P ? kQ_P : 0) |
-                  (args.out_S ? kQ_S : 0) | (args.out_d ? kQ_d : 0) | (args.out_D ? kQ_D : 0);
-    auto launch = [&](auto kernel) {
-        kernel<<<persistent_blocks(kernel, kFusedThreads, needed), kFusedThreads, 0, stream>>>(args);
-        ++g_kernel_launches;
-    };
-    if (args.half_list) {
-        switch (q) {
-            case kQ_P | kQ_S: launch(cell_fused_kernel<T, true, kQ_P | kQ_S>); break;
-            case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
-                launch(cell_fused_kernel<T, true, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>); break;
-            default: launch(cell_fused_kernel<T, true, 0>); break;
-        }
-    } else {
-        switch (q) {
-            case kQ_P | kQ_S: launch(cell_fused_kernel<T, false, kQ_P | kQ_S>); break;
-            case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
-                launch(cell_fused_kernel<T, false, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>); break;
-            case kQ_P | kQ_S | kQ_D: launch(cell_fused_kernel<T, false, kQ_P | kQ_S | kQ_D>); break;
-            default: launch(cell_fused_kernel<T, false, 0>); break;
-        }
-    }
-}
-
-template <typename T>
 void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t stream) {
     if (args.n_brute_atoms == 0) return;
     const int64_t needed = blocks_for(args.n_brute_atoms, kSearchWarps);
     if (write) {
-        brute_search_kernel<T, 1><<<persistent_blocks(brute_search_kernel<T, 1>, kSearchThreads,
-                                                      needed), kSearchThreads, 0, stream>>>(args);
+        brute_search_kernel<T, true><<<persistent_blocks(brute_search_kernel<T, true>,
+                                                         kSearchThreads, needed),
+                                       kSearchThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     } else {
-        brute_search_kernel<T, 0><<<persistent_blocks(brute_search_kernel<T, 0>, kSearchThreads,
-                                                      needed), kSearchThreads, 0, stream>>>(args);
+        brute_search_kernel<T, false><<<persistent_blocks(brute_search_kernel<T, false>,
+                                                          kSearchThreads, needed),
+                                        kSearchThreads, 0, stream>>>(args);
+    ++g_kernel_launches;
     }
-    ++g_kernel_launches;
-}
-
-template <typename T>
-void launch_brute_fused(const SearchArgs<T>& args, cudaStream_t stream) {
-    if (args.n_brute_atoms == 0) return;
-    const int64_t needed = blocks_for(args.n_brute_atoms, kSearchWarps);
-    brute_search_kernel<T, 2><<<persistent_blocks(brute_search_kernel<T, 2>, kSearchThreads, needed),
-                                kSearchThreads, 0, stream>>>(args);
-    ++g_kernel_launches;
 }
 
 size_t scan_workspace_bytes(int64_t n) {
@@ -2238,9 +1908,7 @@ void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* works
     template void launch_cell_search<T>(const SearchArgs<T>&, bool, cudaStream_t);          \
     template void launch_stencil_words<T>(const SearchArgs<T>&, unsigned long long*,      \
                                           cudaStream_t);                                     \
-    template void launch_brute_search<T>(const SearchArgs<T>&, bool, cudaStream_t);          \
-    template void launch_cell_fused<T>(const SearchArgs<T>&, cudaStream_t);                 \
-    template void launch_brute_fused<T>(const SearchArgs<T>&, cudaStream_t);
+    template void launch_brute_search<T>(const SearchArgs<T>&, bool, cudaStream_t);
 TNR_INSTANTIATE(float)
 TNR_INSTANTIATE(double)
 #undef TNR_INSTANTIATE

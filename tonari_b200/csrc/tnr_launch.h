@@ -74,10 +74,6 @@ struct SearchArgs {
     const int32_t* brute_structs; // [n_brute]
     int32_t n_brute;
     int64_t n_brute_atoms;
-    // one-pass emission (unsorted calls): rows are taken from *cursor in
-    // runs, rows at or beyond `capacity` are counted but not written
-    unsigned long long* cursor;
-    int64_t capacity;
     // passes
     uint32_t* counts;           // count pass output
     const int64_t* pair_start;  // write pass input
@@ -173,15 +169,6 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
 
 template <typename T>
 void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t stream);
-
-// One-pass search and emission for unsorted calls: the tests of the count
-// pass and the writes of the write pass in one kernel per mode; every pair
-// takes its output row from args.cursor (order unspecified, as for unsorted
-// calls), so no per-source count, scan or pair-total read precedes it.
-template <typename T>
-void launch_cell_fused(const SearchArgs<T>& args, cudaStream_t stream);
-template <typename T>
-void launch_brute_fused(const SearchArgs<T>& args, cudaStream_t stream);
 
 // Running count of kernels this host thread has launched through this file.
 int64_t launched_kernels();
