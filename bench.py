@@ -198,7 +198,7 @@ def phase_times(lib):
 def host_times(lib):
     buffer = (ctypes.c_double * 12)()
     lib.tnr_last_host_times(buffer, 12)
-    return list(buffer)[:9]
+    return list(buffer)
 
 
 def measure_device(w, steps, warmup, device):
@@ -236,7 +236,7 @@ def measure_device(w, steps, warmup, device):
     finally:
         os.environ.pop("TONARI_B200_PHASE_TIMERS", None)
     median_phase = [statistics.median(p[k] for p in phases) for k in range(6)]
-    median_host = [statistics.median(h[k] for h in hosts) for k in range(9)]
+    median_host = [statistics.median(h[k] for h in hosts) for k in range(12)]
     return {"step_ms": step_ms, "phase_ms": median_phase, "host_ms": median_host,
             "launches": launches, "n_pairs": n_pairs}
 

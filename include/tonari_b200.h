@@ -181,7 +181,9 @@ int tnr_last_phase_times(float* times_ms, int capacity);
  * host thread when TONARI_B200_PHASE_TIMERS=1 is set, else zeros: metadata
  * read, geometry built, prepare launched, extents read back, plans uploaded,
  * ghost totals read back, count pass launched, pair total read back, write
- * pass launched.  Returns the number written (at most 12). */
+ * pass launched, then (marks 9-11, between marks 3 and 4) device geometry
+ * taken over, plans built, bins laid out.  Returns the number written (at
+ * most 12). */
 int tnr_last_host_times(double* times_ms, int capacity);
 
 #ifdef __cplusplus

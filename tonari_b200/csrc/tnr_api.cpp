@@ -536,6 +536,13 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     // the exact host path, which decides results and errors.
     const size_t reduction_bytes = static_cast<size_t>(batch) * sizeof(Reduction<T>);
     const Reduction<T>* reductions = nullptr;
+    const DeviceGeometry* speculated = nullptr;  // device geometry records (speculation)
+    auto dual_of = [&](int64_t b) -> const double* {
+        return speculated ? speculated[b].dual : geometry.duals.data() + 9 * b;
+    };
+    auto repeats_of = [&](int64_t b, int a) -> int64_t {
+        return speculated ? speculated[b].repeats[a] : geometry.repeats[3 * b + a];
+    };
     if (speculate) {
         // Pinned read-back block: extents, two status words, then geometry.
         const size_t geometry_offset = (reduction_bytes + 2 * sizeof(uint32_t) + 255) / 256 * 256;
@@ -554,20 +561,15 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         std::memcpy(status, pinned_read + reduction_bytes, sizeof(status));
         timer.host(3);  // extents and geometry read back
         if (status[0] != 0 || status[1] != 0) throw SpeculationFailed{};
-        geometry.duals.resize(static_cast<size_t>(9 * batch));
-        geometry.repeats.resize(static_cast<size_t>(3 * batch));
+        // The plans read duals and repeats straight from the read-back
+        // records; only the image prefix is built here.
+        speculated = device_geometry;
         geometry.image_begin.assign(static_cast<size_t>(batch + 1), 0);
-        HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
-            for (int64_t b = begin; b < end; ++b) {
-                const DeviceGeometry& g = device_geometry[b];
-                for (int k = 0; k < 9; ++k) geometry.duals[9 * b + k] = g.dual[k];
-                for (int a = 0; a < 3; ++a) geometry.repeats[3 * b + a] = g.repeats[a];
-            }
-        });
         for (int64_t b = 0; b < batch; ++b) {
             geometry.image_begin[b + 1] = geometry.image_begin[b] + device_geometry[b].images;
             if (geometry.image_begin[b + 1] > (int64_t{1} << 24)) throw SpeculationFailed{};
         }
+        timer.host(9);  // device geometry taken over
     }
 
     // ---- per-structure algorithm and plans ---------------------------------
@@ -597,7 +599,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         plan.mode = mode[b];
         plan.image_begin = geometry.image_begin[b];
         plan.n_images = static_cast<int32_t>(geometry.image_begin[b + 1] - geometry.image_begin[b]);
-        for (int a = 0; a < 3; ++a) plan.repeats[a] = geometry.repeats[3 * b + a];
+        for (int a = 0; a < 3; ++a) plan.repeats[a] = static_cast<int32_t>(repeats_of(b, a));
         for (int k = 0; k < 9; ++k) plan.cell[k] = cell_t[9 * b + k];
         plan.cutoff_squared = static_cast<T>(request.cutoff * request.cutoff);
         plan.dims[0] = plan.dims[1] = plan.dims[2] = 1;
@@ -605,7 +607,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     auto plan_cells = [&](int64_t b) {
         if (mode[b] == kModeCell) {
             outcomes[b] = plan_cell(plans[b], reductions[b], cell_t.data() + 9 * b,
-                                    geometry.duals.data() + 9 * b, request.cutoff);
+                                    dual_of(b), request.cutoff);
         }
     };
     HostPool::instance().parallel_for(batch, 256, [&](int64_t begin, int64_t end) {
@@ -615,6 +617,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         }
     });
     const bool any_cell = std::any_of(mode.begin(), mode.end(), [](int32_t m) { return m == kModeCell; });
+    timer.host(10);  // plans built
 
     int64_t total_bins = 0;
     if (any_cell) {
@@ -651,6 +654,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         }
     }
 
+    timer.host(11);  // bins laid out
     // ---- work lists -------------------------------------------------------
     std::vector<int32_t> cell_structs, brute_structs;
     std::vector<int64_t> cell_prefix{0}, brute_prefix{0};
@@ -805,6 +809,18 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.brute_structs = reinterpret_cast<const int32_t*>(second_device + off_brute_structs);
     search.n_brute = static_cast<int32_t>(brute_structs.size());
     search.n_brute_atoms = n_brute_atoms;
+    // Brute-force structures are staged whole in shared memory when every one
+    // of them fits (always under 'auto', whose brute structures have at most
+    // 256 candidates per source).
+    {
+        int64_t largest = 0;
+        for (int32_t b : brute_structs) {
+            const int64_t images = geometry.image_begin[b + 1] - geometry.image_begin[b];
+            largest = std::max<int64_t>(largest, counts[b] * (3 * static_cast<int64_t>(sizeof(T)) + 12) +
+                                                     images * 12);
+        }
+        search.brute_tile_bytes = largest <= 48 * 1024 ? static_cast<int32_t>((largest + 15) / 16 * 16) : 0;
+    }
     search.counts = d_counts;
     search.pair_start = d_pair_start;
     search.index_offset = request.index_offset;
@@ -830,7 +846,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
             build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
         for (int64_t b = 0; b < batch; ++b) {
             for (int a = 0; a < 3; ++a) {
-                if (exact.repeats[3 * b + a] != geometry.repeats[3 * b + a]) throw SpeculationFailed{};
+                if (exact.repeats[3 * b + a] != repeats_of(b, a)) throw SpeculationFailed{};
             }
             if (exact.image_begin[b + 1] != geometry.image_begin[b + 1]) throw SpeculationFailed{};
         }
