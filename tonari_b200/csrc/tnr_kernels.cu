@@ -1570,6 +1570,177 @@ __global__ void __launch_bounds__(kSearchThreads) brute_search_kernel(SearchArgs
     }
 }
 
+// Brute force, tiled: one CTA per brute-force structure (grid-stride over
+// them).  The structure's positions, wraps and image shifts are staged once
+// in shared memory; each warp then takes sources in turn and its lanes
+// stride over the N x I (target, image) candidates, target fastest, reading
+// only shared memory.  Every candidate takes the exact predicate (tonari
+// csrc/core/neighbors_cpu.cpp:222-273).  The write pass queues accepted
+// candidates per warp and emits them 32 at a time into consecutive rows.
+constexpr int kBruteTileThreads = 128;
+constexpr int kBruteTileWarps = kBruteTileThreads / 32;
+constexpr int kBruteTileMaxBytes = 48 * 1024;
+
+template <typename T>
+struct BruteTile {
+    const T* px;
+    const T* py;
+    const T* pz;
+    const int32_t* wx;
+    const int32_t* wy;
+    const int32_t* wz;
+    const int32_t* ix;
+    const int32_t* iy;
+    const int32_t* iz;
+};
+
+template <typename T>
+__device__ __forceinline__ bool brute_tile_evaluate(const BruteTile<T>& tile, const T (&cell)[9],
+                                                    T cutoff_squared, int64_t atom_begin,
+                                                    int32_t s, int32_t t, int32_t image,
+                                                    bool half, bool include_self,
+                                                    long long (&shift)[3], T (&vec)[3]) {
+    shift[0] = static_cast<long long>(tile.ix[image]) - tile.wx[t] + tile.wx[s];
+    shift[1] = static_cast<long long>(tile.iy[image]) - tile.wy[t] + tile.wy[s];
+    shift[2] = static_cast<long long>(tile.iz[image]) - tile.wz[t] + tile.wz[s];
+    vec[0] = vec[1] = vec[2] = T(0);
+    if (!keep_identity(atom_begin + s, atom_begin + t, shift, half, include_self)) return false;
+    if (s == t && shift[0] == 0 && shift[1] == 0 && shift[2] == 0) return true;
+    vec[0] = exact_component(tile.px[t], tile.px[s], shift, cell, 0);
+    vec[1] = exact_component(tile.py[t], tile.py[s], shift, cell, 1);
+    vec[2] = exact_component(tile.pz[t], tile.pz[s], shift, cell, 2);
+    return exact_norm2(vec[0], vec[1], vec[2]) < cutoff_squared;
+}
+
+template <typename T, bool Write>
+__global__ void __launch_bounds__(kBruteTileThreads) brute_tile_kernel(SearchArgs<T> args) {
+    extern __shared__ __align__(16) unsigned char tile_bytes[];
+    __shared__ int2 queue[kBruteTileWarps][64];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const unsigned below = (1u << lane) - 1u;
+    for (int32_t c = blockIdx.x; c < args.n_brute; c += gridDim.x) {
+        const StructurePlan<T>& plan = args.plans[args.brute_structs[c]];
+        const int32_t n = plan.n_atoms;
+        const int32_t images = plan.n_images;
+        const int64_t atom_begin = plan.atom_begin;
+        const int64_t work_begin = args.brute_prefix[c];
+        // Layout: px, py, pz (T[n]); wx, wy, wz (int32[n]); ix, iy, iz (int32[images]).
+        BruteTile<T> tile;
+        T* p = reinterpret_cast<T*>(tile_bytes);
+        int32_t* w = reinterpret_cast<int32_t*>(p + 3 * n);
+        int32_t* im = w + 3 * n;
+        tile.px = p;
+        tile.py = p + n;
+        tile.pz = p + 2 * n;
+        tile.wx = w;
+        tile.wy = w + n;
+        tile.wz = w + 2 * n;
+        tile.ix = im;
+        tile.iy = im + images;
+        tile.iz = im + 2 * images;
+        __syncthreads();  // the previous structure's tile is no longer read
+        for (int32_t k = threadIdx.x; k < n; k += blockDim.x) {
+            const int64_t atom = atom_begin + k;
+            p[k] = args.positions[3 * atom];
+            p[n + k] = args.positions[3 * atom + 1];
+            p[2 * n + k] = args.positions[3 * atom + 2];
+            w[k] = args.wraps[3 * atom];
+            w[n + k] = args.wraps[3 * atom + 1];
+            w[2 * n + k] = args.wraps[3 * atom + 2];
+        }
+        for (int32_t k = threadIdx.x; k < images; k += blockDim.x) {
+            const int4 shift = args.image_shift[plan.image_begin + k];
+            im[k] = shift.x;
+            im[images + k] = shift.y;
+            im[2 * images + k] = shift.z;
+        }
+        T cell[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) cell[k] = plan.cell[k];
+        const T cutoff_squared = plan.cutoff_squared;
+        __syncthreads();
+        const bool half = args.half_list != 0;
+        const bool include_self = args.include_self != 0;
+        const int32_t step_images = 32 / n;
+        const int32_t step_atoms = 32 % n;
+        const int64_t trips = (static_cast<int64_t>(n) * images + 31) / 32;
+        for (int32_t s = warp; s < n; s += kBruteTileWarps) {
+            const int64_t source = atom_begin + s;
+            const int64_t order = args.source_order ? args.n_sources + work_begin + s : source;
+            int64_t out_row = 0;
+            if constexpr (Write) {
+                if (args.counts[order] == 0) continue;
+                out_row = args.pair_start[order];
+            }
+            int32_t t = lane % n;
+            int32_t image = lane / n;
+            uint32_t count = 0;
+            int32_t queued = 0;
+            for (int64_t trip = 0; trip < trips; ++trip) {
+                bool accept = false;
+                long long shift[3];
+                T vec[3];
+                if (image < images) {
+                    accept = brute_tile_evaluate(tile, cell, cutoff_squared, atom_begin, s, t, image,
+                                                 half, include_self, shift, vec);
+                    if (!Write && accept) {
+                        if (shift[0] < INT_MIN || shift[0] > INT_MAX || shift[1] < INT_MIN ||
+                            shift[1] > INT_MAX || shift[2] < INT_MIN || shift[2] > INT_MAX) {
+                            atomicOr(args.status, static_cast<uint32_t>(kStatusShiftRange));
+                        }
+                    }
+                }
+                const unsigned ballot = __ballot_sync(kFullMask, accept);
+                if constexpr (Write) {
+                    if (ballot) {
+                        int2* q = queue[warp];
+                        if (accept) q[queued + __popc(ballot & below)] = make_int2(t, image);
+                        queued += __popc(ballot);
+                        if (queued >= 32) {
+                            __syncwarp();
+                            const int2 item = q[lane];
+                            brute_tile_evaluate(tile, cell, cutoff_squared, atom_begin, s, item.x,
+                                                item.y, half, include_self, shift, vec);
+                            emit_pair(args, out_row + lane, source, atom_begin + item.x, shift, vec);
+                            __syncwarp();
+                            if (lane < queued - 32) q[lane] = q[32 + lane];
+                            __syncwarp();
+                            queued -= 32;
+                            out_row += 32;
+                        }
+                    }
+                } else {
+                    count += __popc(ballot);
+                }
+                t += step_atoms;
+                image += step_images;
+                if (t >= n) {
+                    t -= n;
+                    ++image;
+                }
+            }
+            if constexpr (Write) {
+                __syncwarp();
+                if (lane < queued) {
+                    const int2 item = queue[warp][lane];
+                    long long shift[3];
+                    T vec[3];
+                    brute_tile_evaluate(tile, cell, cutoff_squared, atom_begin, s, item.x, item.y,
+                                        half, include_self, shift, vec);
+                    emit_pair(args, out_row + lane, source, atom_begin + item.x, shift, vec);
+                }
+                __syncwarp();
+            } else if (lane == 0) {
+                args.counts[order] = count;
+                if (count > static_cast<uint32_t>(INT_MAX)) {
+                    atomicOr(args.status, static_cast<uint32_t>(kStatusCountRange));
+                }
+            }
+        }
+    }
+}
+
 // Candidate filter for Verlet-skin reuse: thread per candidate pair; the
 // decisive test is the one of the search kernels (exact_component in the
 // reference's order, exact_norm2 < (T)(cutoff^2)).  Pass 1 stores one ballot
@@ -1697,6 +1868,16 @@ int64_t blocks_for(int64_t items, int64_t per_block) { return (items + per_block
 
 // Grid for a grid-stride kernel: enough blocks to fill every SM at the
 // kernel's occupancy, never more than the work needs.
+template <typename Kernel>
+unsigned persistent_blocks_smem(Kernel kernel, int threads, size_t dynamic_bytes, int64_t needed) {
+    int device = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, dynamic_bytes);
+    const int64_t full = static_cast<int64_t>(sms) * std::max(per_sm, 1);
+    return static_cast<unsigned>(std::max<int64_t>(1, std::min(needed, full)));
+}
+
 template <typename Kernel>
 unsigned persistent_blocks(Kernel kernel, int threads, int64_t needed) {
     int device = 0, sms = 148, per_sm = 1;
@@ -1846,6 +2027,20 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
 template <typename T>
 void launch_brute_search(const SearchArgs<T>& args, bool write, cudaStream_t stream) {
     if (args.n_brute_atoms == 0) return;
+    if (args.brute_tile_bytes > 0 && args.brute_tile_bytes <= kBruteTileMaxBytes) {
+        const size_t bytes = static_cast<size_t>(args.brute_tile_bytes);
+        if (write) {
+            brute_tile_kernel<T, true><<<persistent_blocks_smem(brute_tile_kernel<T, true>,
+                                                                kBruteTileThreads, bytes, args.n_brute),
+                                         kBruteTileThreads, bytes, stream>>>(args);
+        } else {
+            brute_tile_kernel<T, false><<<persistent_blocks_smem(brute_tile_kernel<T, false>,
+                                                                 kBruteTileThreads, bytes, args.n_brute),
+                                          kBruteTileThreads, bytes, stream>>>(args);
+        }
+        ++g_kernel_launches;
+        return;
+    }
     const int64_t needed = blocks_for(args.n_brute_atoms, kSearchWarps);
     if (write) {
         brute_search_kernel<T, true><<<persistent_blocks(brute_search_kernel<T, true>,

@@ -74,6 +74,10 @@ struct SearchArgs {
     const int32_t* brute_structs; // [n_brute]
     int32_t n_brute;
     int64_t n_brute_atoms;
+    // Shared-memory bytes one brute-force structure needs staged (positions,
+    // wraps, image shifts) when every brute structure fits a CTA; 0 selects
+    // the kernel that reads them from global memory.
+    int32_t brute_tile_bytes;
     // passes
     uint32_t* counts;           // count pass output
     const int64_t* pair_start;  // write pass input
