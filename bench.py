@@ -297,10 +297,15 @@ def cpu_reference_rate(w, threads=None):
             "structures_per_s": w.n_structures / seconds}
 
 
-# DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
-# captures summarised in profiles/ (the capture command is in each summary),
-# per emitted pair, keyed by (workload, phase).
-TRAFFIC_PER_PAIR = {}
+# DRAM bytes (read + write) of the dominant kernel per emitted pair, keyed by
+# (workload, phase), from one ncu capture of that kernel on a reduced case of
+# the same workload; `traffic` scales it by the call's pairs.  Sources:
+#   cfg4 write pass: profiles/cell_emit_cfg4_200k.md (45.6 MB + 738.6 MB for
+#     18,104,094 pairs at 200,000 atoms);
+#   cfg5 count pass: profiles/cell_count_cfg5_512.md (49.3 MB + 2.1 MB for
+#     11,101,838 half pairs at 512 structures).
+TRAFFIC_PER_PAIR = {("cfg4", "write"): 784.189184e6 / 18_104_094,
+                    ("cfg5", "count"): 51.445248e6 / 11_101_838}
 
 
 def roofline(w, n_pairs, phase_ms, step_ms):
