@@ -1594,12 +1594,25 @@ struct BruteTile {
     const int32_t* iz;
 };
 
+// `plain`: a structure without periodic axes has one image and zero wraps,
+// so every shift is zero and the public displacement is p_t - p_s (adding
+// the zero translation changes at most the sign of a zero component).
 template <typename T>
 __device__ __forceinline__ bool brute_tile_evaluate(const BruteTile<T>& tile, const T (&cell)[9],
                                                     T cutoff_squared, int64_t atom_begin,
                                                     int32_t s, int32_t t, int32_t image,
-                                                    bool half, bool include_self,
+                                                    bool half, bool include_self, bool plain,
                                                     long long (&shift)[3], T (&vec)[3]) {
+    if (plain) {
+        shift[0] = shift[1] = shift[2] = 0;
+        vec[0] = vec[1] = vec[2] = T(0);
+        if (s == t) return include_self;
+        if (half && s > t) return false;
+        vec[0] = sub_rn(tile.px[t], tile.px[s]);
+        vec[1] = sub_rn(tile.py[t], tile.py[s]);
+        vec[2] = sub_rn(tile.pz[t], tile.pz[s]);
+        return exact_norm2(vec[0], vec[1], vec[2]) < cutoff_squared;
+    }
     shift[0] = static_cast<long long>(tile.ix[image]) - tile.wx[t] + tile.wx[s];
     shift[1] = static_cast<long long>(tile.iy[image]) - tile.wy[t] + tile.wy[s];
     shift[2] = static_cast<long long>(tile.iz[image]) - tile.wz[t] + tile.wz[s];
@@ -1662,6 +1675,7 @@ __global__ void __launch_bounds__(kBruteTileThreads) brute_tile_kernel(SearchArg
         __syncthreads();
         const bool half = args.half_list != 0;
         const bool include_self = args.include_self != 0;
+        const bool plain = images == 1;
         const int32_t step_images = 32 / n;
         const int32_t step_atoms = 32 % n;
         const int64_t trips = (static_cast<int64_t>(n) * images + 31) / 32;
@@ -1683,7 +1697,7 @@ __global__ void __launch_bounds__(kBruteTileThreads) brute_tile_kernel(SearchArg
                 T vec[3];
                 if (image < images) {
                     accept = brute_tile_evaluate(tile, cell, cutoff_squared, atom_begin, s, t, image,
-                                                 half, include_self, shift, vec);
+                                                 half, include_self, plain, shift, vec);
                     if (!Write && accept) {
                         if (shift[0] < INT_MIN || shift[0] > INT_MAX || shift[1] < INT_MIN ||
                             shift[1] > INT_MAX || shift[2] < INT_MIN || shift[2] > INT_MAX) {
@@ -1701,7 +1715,7 @@ __global__ void __launch_bounds__(kBruteTileThreads) brute_tile_kernel(SearchArg
                             __syncwarp();
                             const int2 item = q[lane];
                             brute_tile_evaluate(tile, cell, cutoff_squared, atom_begin, s, item.x,
-                                                item.y, half, include_self, shift, vec);
+                                                item.y, half, include_self, plain, shift, vec);
                             emit_pair(args, out_row + lane, source, atom_begin + item.x, shift, vec);
                             __syncwarp();
                             if (lane < queued - 32) q[lane] = q[32 + lane];
@@ -1727,7 +1741,7 @@ __global__ void __launch_bounds__(kBruteTileThreads) brute_tile_kernel(SearchArg
                     long long shift[3];
                     T vec[3];
                     brute_tile_evaluate(tile, cell, cutoff_squared, atom_begin, s, item.x, item.y,
-                                        half, include_self, shift, vec);
+                                        half, include_self, plain, shift, vec);
                     emit_pair(args, out_row + lane, source, atom_begin + item.x, shift, vec);
                 }
                 __syncwarp();
