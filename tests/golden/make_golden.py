@@ -1,8 +1,9 @@
 """Generate tests/golden/*.npz from the reference implementation.
 
-Run in a container that has the reference checkout (default /root/reference):
+Run where the reference checkout is available, naming it with --reference or
+the TONARI_REFERENCE_ROOT environment variable:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 For every case the expected pair set comes from the reference's independent
 Torch oracle (tests/support/reference.py, ``neighbor_list_reference``), and is
@@ -14,6 +15,7 @@ access to the reference.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import sys
 from pathlib import Path
@@ -73,8 +75,10 @@ def cases():
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("TONARI_REFERENCE_ROOT"))
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("name the reference checkout with --reference or TONARI_REFERENCE_ROOT")
     reference = load_reference_oracle(Path(args.reference))
     from oracle import oracle
 

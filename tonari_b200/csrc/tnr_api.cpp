@@ -685,7 +685,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     unsigned long long* d_bin_start = nullptr;
     V4* d_ghost_pos = nullptr;
     int4* d_ghost_meta = nullptr;
-    int32_t* d_self_slot = nullptr;
     int32_t* d_source_list = nullptr;
     int32_t* d_source_bin = nullptr;
     uint32_t* d_mask_words = nullptr;
@@ -701,6 +700,10 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     bin_args.wraps = d_wraps;
     bin_args.wrapped = d_wrapped;
     bin_args.status = d_status;
+    // Unsorted calls test each unordered pair once (cell-order output);
+    // sorted calls search every source's full stencil.
+    const bool pair_once = !request.sorted;
+    bin_args.pair_once = pair_once ? 1 : 0;
     const int64_t total_images = geometry.image_begin[batch];
     auto* d_image_shift = workspace.get<int4>(std::max<int64_t>(total_images, 1));
     auto* d_image_translation = workspace.get<V4>(std::max<int64_t>(total_images, 1));
@@ -736,6 +739,8 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         words_args.n_cell = bin_args.n_cell;
         words_args.n_bins = total_bins;
         words_args.bin_struct = d_bin_struct;
+        words_args.n_sources = n_cell_atoms;
+        words_args.pair_once = bin_args.pair_once;
         auto* d_bin_words = workspace.get<unsigned long long>(total_bins);
         d_bin_word_start = workspace.get<unsigned long long>(total_bins + 1);
         launch_stencil_words(words_args, d_bin_words, stream);
@@ -754,15 +759,14 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         timer.host(5);  // ghost and mask totals read back
         require_search(mask_words < (1ull << 32), "cell-list candidate bitmask exceeds uint32 indexing");
         d_mask_words = workspace.get<uint32_t>(mask_words);
-        const int64_t ghosts = static_cast<int64_t>(packed_total & 0xffffffffull);
+        // Ghost slots: the sources' zero images, then the other copies.
         const int64_t sources = static_cast<int64_t>(packed_total >> 32);
-        require_search(sources == n_cell_atoms && ghosts >= sources &&
-                           ghosts < std::numeric_limits<int32_t>::max(),
+        const int64_t ghosts = sources + static_cast<int64_t>(packed_total & 0xffffffffull);
+        require_search(sources == n_cell_atoms && ghosts < std::numeric_limits<int32_t>::max(),
                        "cell-list image copies exceed int32 indexing");
         d_ghost_pos = workspace.get<V4>(ghosts);
         d_ghost_meta = workspace.get<int4>(ghosts);
         if (request.quantities & (TNR_Q_d | TNR_Q_D)) d_ghost_orig = workspace.get<V4>(ghosts);
-        d_self_slot = workspace.get<int32_t>(n_atoms);
         d_source_list = workspace.get<int32_t>(n_cell_atoms);
         d_source_bin = workspace.get<int32_t>(n_cell_atoms);
         bin_args.bin_counts = d_cursor;
@@ -770,7 +774,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         bin_args.ghost_meta = d_ghost_meta;
         bin_args.ghost_orig = d_ghost_orig;
         bin_args.positions = static_cast<const T*>(request.positions);
-        bin_args.self_slot = d_self_slot;
         bin_args.source_list = d_source_list;
         bin_args.source_bin = d_source_bin;
         launch_bin(bin_args, true, stream);
@@ -791,7 +794,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.bin_start = d_bin_start;
     search.ghost_pos = d_ghost_pos;
     search.ghost_meta = d_ghost_meta;
-    search.self_slot = d_self_slot;
     search.source_list = d_source_list;
     search.source_bin = d_source_bin;
     search.n_sources = n_cell_atoms;
@@ -805,6 +807,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.bin_struct = d_bin_struct;
     search.ghost_orig = d_ghost_orig;
     search.source_order = request.sorted ? 0 : 1;
+    search.pair_once = bin_args.pair_once;
     search.brute_prefix = reinterpret_cast<const int64_t*>(second_device + off_brute_prefix);
     search.brute_structs = reinterpret_cast<const int32_t*>(second_device + off_brute_structs);
     search.n_brute = static_cast<int32_t>(brute_structs.size());

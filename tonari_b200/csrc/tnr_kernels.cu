@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <climits>
 #include <cstdint>
+#include <type_traits>
 
 #include "tnr_kernels.cuh"
 #include "tnr_launch.h"
@@ -384,10 +385,19 @@ __global__ void __launch_bounds__(kPrepareThreads) verify_wraps_kernel(
 // One thread per atom of a cell-list structure, looping over the structure's
 // images.  An image copy is kept when it lies inside the structure's culling
 // box (extent of the wrapped atoms padded by the search radius), the
-// reference's rule (tonari csrc/core/neighbors_cpu.cpp:479-495).  The zero
-// image is always inside.  Each bin counter packs (sources << 32 | ghosts),
-// so one 64-bit atomic hands out both the ghost slot and, for the zero image,
-// the source slot.
+// reference's rule (tonari csrc/core/neighbors_cpu.cpp:479-495).  Ghost
+// records live in two regions of one array: the zero images (the sources)
+// at [0, S) in source-slot order and the other image copies at [S, S + I).
+// Each bin counter packs (sources << 32 | image copies), so one 64-bit
+// atomic hands out the slot in either region.  The zero image is placed
+// first so that the atom's other copies carry its source slot.
+//
+// Pair-once calls (args.pair_once) test every unordered pair from one side
+// only: from source s, candidate copy c of atom t is tested when
+// slot(t) > slot(s) (ties: the canonical shift).  Source slots follow the bin
+// order, so a copy whose atom's home bin lies below every bin of its own
+// stencil neighbourhood (bin - (d1 d2 + d2 + 1) in the row-major order) can
+// never be tested and is not kept.
 template <typename T, bool Scatter>
 __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
     using V = vec4_t<T>;
@@ -420,52 +430,67 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
     const T origin[3] = {plan.origin[0], plan.origin[1], plan.origin[2]};
     const T inv_edge = plan.inv_edge;
     const V* translations = reinterpret_cast<const V*>(args.image_translation) + image_begin;
-    for (int32_t k = 0; k < n_images; ++k) {
-        const V tr = translations[k];
-        T g[3];
-        g[0] = add_rn(q.x, tr.x);
-        g[1] = add_rn(q.y, tr.y);
-        g[2] = add_rn(q.z, tr.z);
-        const bool inside = g[0] >= lower[0] && g[0] <= upper[0] &&
-                            g[1] >= lower[1] && g[1] <= upper[1] &&
-                            g[2] >= lower[2] && g[2] <= upper[2];
-        if (!inside && k != center) continue;
+    auto bin_of = [&](const T (&g)[3]) -> int64_t {
         const int32_t bx = bin_axis(g[0], origin[0], inv_edge, dims[0]);
         const int32_t by = bin_axis(g[1], origin[1], inv_edge, dims[1]);
         const int32_t bz = bin_axis(g[2], origin[2], inv_edge, dims[2]);
-        const int64_t bin = bin_begin +
-            (static_cast<int64_t>(bx) * dims[1] + by) * dims[2] + bz;
-        const unsigned long long increment =
-            k == center ? (1ull << 32) + 1ull : 1ull;
-        const unsigned long long old = atomicAdd(&args.bin_counts[bin], increment);
+        return bin_begin + (static_cast<int64_t>(bx) * dims[1] + by) * dims[2] + bz;
+    };
+    auto store = [&](uint32_t slot, const T (&g)[3], int32_t k, uint32_t key) {
+        V record;
+        record.x = g[0];
+        record.y = g[1];
+        record.z = g[2];
+        record.w = index_to_lane(static_cast<int32_t>(key), T(0));
+        reinterpret_cast<V*>(args.ghost_pos)[slot] = record;
+        if (args.ghost_orig) {  // only the d / D outputs read it
+            V original;
+            original.x = args.positions[3 * atom];
+            original.y = args.positions[3 * atom + 1];
+            original.z = args.positions[3 * atom + 2];
+            original.w = index_to_lane(static_cast<int32_t>(atom), T(0));
+            reinterpret_cast<V*>(args.ghost_orig)[slot] = original;
+        }
+        const int4 image = args.image_shift[image_begin + k];
+        args.ghost_meta[slot] = make_int4(image.x - wrap[0], image.y - wrap[1], image.z - wrap[2],
+                                          static_cast<int32_t>(atom));
+    };
+    // Zero image: the source.
+    int64_t home;
+    uint32_t key_base;  // order key base: 2 * (source slot or atom)
+    {
+        const V tr = translations[center];
+        const T g[3] = {add_rn(q.x, tr.x), add_rn(q.y, tr.y), add_rn(q.z, tr.z)};
+        home = bin_of(g);
+        const unsigned long long old = atomicAdd(&args.bin_counts[home], 1ull << 32);
+        const uint32_t source_slot = static_cast<uint32_t>(old >> 32);
+        key_base = 2u * (args.pair_once ? source_slot : static_cast<uint32_t>(atom));
         if constexpr (Scatter) {
-            const uint32_t slot = static_cast<uint32_t>(old & 0xffffffffull);
-            V record;
-            record.x = g[0];
-            record.y = g[1];
-            record.z = g[2];
-            // Order key of the image (2a + 1 for the zero image, 2a + 2
-            // otherwise; read by the search kernels).
-            record.w = index_to_lane(static_cast<int32_t>(2u * static_cast<uint32_t>(atom) +
-                                                          (k == center ? 1u : 2u)),
-                                     T(0));
-            reinterpret_cast<V*>(args.ghost_pos)[slot] = record;
-            if (args.ghost_orig) {  // only the d / D outputs read it
-                V original;
-                original.x = args.positions[3 * atom];
-                original.y = args.positions[3 * atom + 1];
-                original.z = args.positions[3 * atom + 2];
-                original.w = index_to_lane(static_cast<int32_t>(atom), T(0));
-                reinterpret_cast<V*>(args.ghost_orig)[slot] = original;
-            }
-            const int4 image = args.image_shift[image_begin + k];
-            args.ghost_meta[slot] = make_int4(image.x - wrap[0], image.y - wrap[1],
-                                              image.z - wrap[2], static_cast<int32_t>(atom));
-            if (k == center) {
-                args.source_list[static_cast<uint32_t>(old >> 32)] = static_cast<int32_t>(atom);
-                args.source_bin[static_cast<uint32_t>(old >> 32)] = static_cast<int32_t>(bin);
-                args.self_slot[atom] = static_cast<int32_t>(slot);
-            }
+            // Order key of the copy: 2a + 1 for the zero image, 2a + 2 for
+            // the others (a = source slot or atom; read by the search).
+            store(source_slot, g, center, key_base + 1u);
+            args.source_list[source_slot] = static_cast<int32_t>(atom);
+            args.source_bin[source_slot] = static_cast<int32_t>(home);
+        }
+    }
+    // Pair-once: a copy in a bin above home + (d1 d2 + d2 + 1) has its atom's
+    // home below every bin of its stencil neighbourhood.
+    const int64_t highest_kept = args.pair_once
+        ? home + static_cast<int64_t>(dims[1]) * dims[2] + dims[2] + 1 : INT64_MAX;
+    for (int32_t k = 0; k < n_images; ++k) {
+        if (k == center) continue;
+        const V tr = translations[k];
+        const T g[3] = {add_rn(q.x, tr.x), add_rn(q.y, tr.y), add_rn(q.z, tr.z)};
+        const bool inside = g[0] >= lower[0] && g[0] <= upper[0] &&
+                            g[1] >= lower[1] && g[1] <= upper[1] &&
+                            g[2] >= lower[2] && g[2] <= upper[2];
+        if (!inside) continue;
+        const int64_t bin = bin_of(g);
+        if (bin > highest_kept) continue;
+        const unsigned long long old = atomicAdd(&args.bin_counts[bin], 1ull);
+        if constexpr (Scatter) {
+            store(static_cast<uint32_t>(args.n_cell_atoms) + static_cast<uint32_t>(old & 0xffffffffull),
+                  g, k, key_base + 2u);
         }
     }
 }
@@ -514,20 +539,32 @@ __device__ __forceinline__ void exact_displacement(const T* __restrict__ positio
 
 // ---- cell list -------------------------------------------------------------
 //
-// One warp per bin: the bin's 27-bin stencil is loaded once (nine z-rows,
-// each a contiguous slot range of the cell-sorted ghost array) and the warp
-// then serves every source atom of the bin in turn.  For one source the warp
-// walks the concatenated rows 32 candidates per iteration; each lane keeps
-// its own (row, slot) cursor and advances it by 32, and the next iteration's
-// record is loaded before the current one is evaluated so that two loads are
-// in flight per lane.  Candidate k of a source is lane k % 32 of iteration
-// k / 32 in both passes, so the count pass hands its per-iteration ballots to
-// the write pass as a bitmask at a deterministic offset:
+// One warp per bin: the bin's 27-bin stencil is loaded once and the warp then
+// serves every source atom of the bin in turn.  Each of the nine z-rows of
+// the stencil is two contiguous slot ranges, one in the zero-image region
+// (the sources of those bins) and one in the image-copy region, so a stencil
+// is a list of ranges that the search walks as one flattened candidate
+// sequence, 32 candidates per tile.  Candidate k of a source is lane k % 32
+// of tile k / 32 in both passes, so the count pass hands its per-tile
+// ballots to the write pass as a bitmask at a deterministic offset:
 //   bin_word_start[bin] + (source rank in bin) * ceil(candidates / 32).
+//
+// Pair-once stencils (PairOnce = true) drop the zero-image ranges that can
+// hold no tested candidate: rows before the source's own row lie in lower
+// bins (lower source slots), and the source's own row starts at its bin.
 
+template <bool PairOnce>
+struct StencilShape {
+    static constexpr int kZeroRanges = PairOnce ? 5 : 9;
+    static constexpr int kRanges = kZeroRanges + 9;
+    static constexpr int kTable = PairOnce ? 16 : 32;  // power of two > kRanges
+};
+
+template <bool PairOnce>
 struct StencilRows {
-    int32_t prefix[16];  // candidate index where row r starts; [9] = total; [10..] = INT_MAX
-    int32_t delta[9];    // slot = candidate index + delta[row]
+    int32_t prefix[StencilShape<PairOnce>::kTable];  // candidate index where range r
+                                                     // starts; [kRanges] = total, then INT_MAX
+    int32_t delta[StencilShape<PairOnce>::kRanges];  // slot = candidate index + delta[range]
 };
 
 template <typename T>
@@ -542,46 +579,90 @@ __device__ __forceinline__ void bin_coordinates(const StructurePlan<T>& plan, in
     bx = static_cast<int32_t>(plane);
 }
 
-// Lanes 0-8 fetch the slot range of one stencil row each and the warp builds
-// the row prefix table (into `rows` when non-null); returns the total
-// candidate count (warp-uniform).
-template <typename T>
-__device__ __forceinline__ int32_t load_stencil(const StructurePlan<T>& plan,
-                                                const unsigned long long* __restrict__ bin_start,
-                                                int32_t bx, int32_t by, int32_t bz,
-                                                StencilRows* rows, int lane) {
-    int32_t begin = 0, length = 0;
-    if (lane < 9) {
-        const int32_t x = bx + lane / 3 - 1;
-        const int32_t y = by + lane % 3 - 1;
-        if (x >= 0 && x < plan.dims[0] && y >= 0 && y < plan.dims[1]) {
-            const int32_t z0 = max(bz - 1, 0);
-            const int32_t z1 = min(bz + 1, plan.dims[2] - 1);
-            const int64_t row = plan.bin_begin +
-                (static_cast<int64_t>(x) * plan.dims[1] + y) * plan.dims[2];
-            begin = static_cast<int32_t>(bin_start[row + z0] & 0xffffffffull);
-            length = static_cast<int32_t>(bin_start[row + z1 + 1] & 0xffffffffull) - begin;
+// Range r of the stencil of bin (bx, by, bz): first ghost slot and length.
+// Ranges [0, kZeroRanges) are zero-image ranges of rows (PairOnce: 4..8,
+// else 0..8), the rest the image-copy ranges of rows 0..8; row = 3 dx + dy.
+template <bool PairOnce, typename T>
+__device__ __forceinline__ void stencil_range(const StructurePlan<T>& plan,
+                                              const unsigned long long* __restrict__ bin_start,
+                                              int64_t n_sources, int32_t bx, int32_t by,
+                                              int32_t bz, int r, int32_t& begin, int32_t& length) {
+    constexpr int kZero = StencilShape<PairOnce>::kZeroRanges;
+    const bool zero = r < kZero;
+    const int row = zero ? (PairOnce ? r + 4 : r) : r - kZero;
+    begin = 0;
+    length = 0;
+    const int32_t x = bx + row / 3 - 1;
+    const int32_t y = by + row % 3 - 1;
+    if (x >= 0 && x < plan.dims[0] && y >= 0 && y < plan.dims[1]) {
+        const int32_t z0 = (PairOnce && zero && row == 4) ? bz : max(bz - 1, 0);
+        const int32_t z1 = min(bz + 1, plan.dims[2] - 1);
+        const int64_t line = plan.bin_begin + (static_cast<int64_t>(x) * plan.dims[1] + y) * plan.dims[2];
+        const unsigned long long lo = bin_start[line + z0];
+        const unsigned long long hi = bin_start[line + z1 + 1];
+        if (zero) {
+            begin = static_cast<int32_t>(lo >> 32);
+            length = static_cast<int32_t>(hi >> 32) - begin;
+        } else {
+            begin = static_cast<int32_t>(n_sources) + static_cast<int32_t>(lo & 0xffffffffull);
+            length = static_cast<int32_t>(hi & 0xffffffffull) - static_cast<int32_t>(lo & 0xffffffffull);
         }
     }
+}
+
+// Lanes fetch one stencil range each and the warp builds the prefix table
+// (into `rows` when non-null); returns the total candidate count
+// (warp-uniform).
+template <bool PairOnce, typename T>
+__device__ __forceinline__ int32_t load_stencil(const StructurePlan<T>& plan,
+                                                const unsigned long long* __restrict__ bin_start,
+                                                int64_t n_sources, int32_t bx, int32_t by,
+                                                int32_t bz, StencilRows<PairOnce>* rows, int lane) {
+    constexpr int kRanges = StencilShape<PairOnce>::kRanges;
+    constexpr int kTable = StencilShape<PairOnce>::kTable;
+    int32_t begin = 0, length = 0;
+    if (lane < kRanges) stencil_range<PairOnce>(plan, bin_start, n_sources, bx, by, bz, lane, begin, length);
     int32_t inclusive = length;
 #pragma unroll
-    for (int offset = 1; offset < 16; offset <<= 1) {
+    for (int offset = 1; offset < 32; offset <<= 1) {
         const int32_t other = __shfl_up_sync(kFullMask, inclusive, offset);
         if (lane >= offset) inclusive += other;
     }
-    const int32_t total = __shfl_sync(kFullMask, inclusive, 8);
+    const int32_t total = __shfl_sync(kFullMask, inclusive, kRanges - 1);
     if (rows) {
-        if (lane < 9) {
+        if (lane < kRanges) {
             rows->prefix[lane] = inclusive - length;
             rows->delta[lane] = begin - (inclusive - length);
-        } else if (lane == 9) {
-            rows->prefix[9] = total;
-        } else if (lane < 16) {
+        } else if (lane == kRanges) {
+            rows->prefix[lane] = total;
+        } else if (lane < kTable) {
             rows->prefix[lane] = INT_MAX;
         }
     }
     __syncwarp();
     return total;
+}
+
+// The same table built by one thread; returns the total.
+template <bool PairOnce, typename T>
+__device__ __forceinline__ int32_t build_stencil(const StructurePlan<T>& plan,
+                                                 const unsigned long long* __restrict__ bin_start,
+                                                 int64_t n_sources, int32_t bx, int32_t by,
+                                                 int32_t bz, StencilRows<PairOnce>& rows) {
+    constexpr int kRanges = StencilShape<PairOnce>::kRanges;
+    int32_t prefix = 0;
+#pragma unroll
+    for (int r = 0; r < kRanges; ++r) {
+        int32_t begin, length;
+        stencil_range<PairOnce>(plan, bin_start, n_sources, bx, by, bz, r, begin, length);
+        rows.prefix[r] = prefix;
+        rows.delta[r] = begin - prefix;
+        prefix += length;
+    }
+    rows.prefix[kRanges] = prefix;
+#pragma unroll
+    for (int r = kRanges + 1; r < StencilShape<PairOnce>::kTable; ++r) rows.prefix[r] = INT_MAX;
+    return prefix;
 }
 
 // Position of the (n+1)-th set bit of w (0 <= n < popc(w)), by halving.
@@ -602,21 +683,22 @@ __device__ __forceinline__ int32_t nth_set_bit(uint32_t w, int32_t n) {
     return position;
 }
 
-// Slot of candidate index k (0 <= k < total): the last row whose prefix is
-// <= k, found in four fixed steps.
-__device__ __forceinline__ int32_t slot_of(const StencilRows& rows, int32_t k) {
+// Slot of candidate index k (0 <= k < total): the last range whose prefix is
+// <= k, found by halving the power-of-two table.
+template <bool PairOnce>
+__device__ __forceinline__ int32_t slot_of(const StencilRows<PairOnce>& rows, int32_t k) {
     int32_t r = 0;
-    r += (rows.prefix[r + 8] <= k) ? 8 : 0;
-    r += (rows.prefix[r + 4] <= k) ? 4 : 0;
-    r += (rows.prefix[r + 2] <= k) ? 2 : 0;
-    r += (rows.prefix[r + 1] <= k) ? 1 : 0;
+#pragma unroll
+    for (int step = StencilShape<PairOnce>::kTable / 2; step > 0; step >>= 1) {
+        r += (rows.prefix[r + step] <= k) ? step : 0;
+    }
     return k + rows.delta[r];
 }
 
 
 // Per bin: bitmask words of all its sources (sources * ceil(candidates / 32)).
-// One thread per bin; its 18 row-bound loads are independent.
-template <typename T>
+// One thread per bin; its row-bound loads are independent.
+template <bool PairOnce, typename T>
 __global__ void __launch_bounds__(kBinThreads) stencil_words_kernel(SearchArgs<T> args,
                                                                     int64_t n_bins,
                                                                     unsigned long long* bin_words) {
@@ -630,18 +712,12 @@ __global__ void __launch_bounds__(kBinThreads) stencil_words_kernel(SearchArgs<T
     const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
     int32_t bx, by, bz;
     bin_coordinates(plan, bin, bx, by, bz);
-    const int32_t z0 = max(bz - 1, 0);
-    const int32_t z1 = min(bz + 1, plan.dims[2] - 1);
     int64_t total = 0;
 #pragma unroll
-    for (int r = 0; r < 9; ++r) {
-        const int32_t x = bx + r / 3 - 1;
-        const int32_t y = by + r % 3 - 1;
-        if (x >= 0 && x < plan.dims[0] && y >= 0 && y < plan.dims[1]) {
-            const int64_t row = plan.bin_begin + (static_cast<int64_t>(x) * plan.dims[1] + y) * plan.dims[2];
-            total += static_cast<int64_t>(args.bin_start[row + z1 + 1] & 0xffffffffull) -
-                     static_cast<int64_t>(args.bin_start[row + z0] & 0xffffffffull);
-        }
+    for (int r = 0; r < StencilShape<PairOnce>::kRanges; ++r) {
+        int32_t begin, length;
+        stencil_range<PairOnce>(plan, args.bin_start, args.n_sources, bx, by, bz, r, begin, length);
+        total += length;
     }
     bin_words[bin] = sources * static_cast<unsigned long long>((total + 31) >> 5);
 }
@@ -703,16 +779,19 @@ __device__ __forceinline__ uint32_t transpose_bits32(uint32_t x, int lane) {
 // transpose across the warp then gives every source its mask word for the
 // tile.  The lanes stay busy whatever the bin's source count.
 //
-// Half lists compare order keys instead of atom indices.  The ghost record's
-// fourth lane carries key 2a + 1 for the zero image of atom a and 2a + 2 for
-// its other images (written by the scatter); a source's key is 2a + 1.
-// Key(c) > key(s) + 1 means atom(c) > atom(s) (accepted by distance alone),
+// Half lists and pair-once calls compare order keys.  The ghost record's
+// fourth lane carries key 2a + 1 for the zero image of a and 2a + 2 for its
+// other images (written by the scatter), a = the atom, or for pair-once
+// calls the atom's source slot; a source's key is 2a + 1.
+// Key(c) > key(s) + 1 means a(c) > a(s) (accepted by distance alone),
 // tested as the sign of (key(s) + 1) - key(c); key(c) == key(s) + 1 is a
 // periodic image of the source itself (decided by its shift in the rare
 // path); key(c) == key(s) is the zero-shift self pair, which the test neither
 // accepts nor flags and which is set afterwards per include_self.
 // Full lists accept the self pair by distance (d = 0) and fix it the same
-// way.  Candidates in the band shell are flagged per lane and the flagged
+// way.  Pair-once calls leave it out of the bitmask and count it per
+// include_self; a pair-once half list emits each accepted pair once in its
+// canonical orientation, a full list emits it in both.  Candidates in the band shell are flagged per lane and the flagged
 // lanes decide them exactly.
 // Accepted-candidate bits are stored transposed -- word w of source rank r at
 // base + w * S + r, S the bin's source count -- one coalesced store per tile.
@@ -742,16 +821,18 @@ __device__ __forceinline__ uint32_t push_key(uint32_t bits, uint32_t source_key_
     return __funnelshift_l(source_key_plus_one - candidate_key, bits, 1);
 }
 
-template <typename T, bool Half>
+template <typename T, bool Half, bool PairOnce>
 __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
-    __shared__ StencilRows stencil[kSearchWarps];
+    constexpr bool Keyed = Half || PairOnce;
+    __shared__ StencilRows<PairOnce> stencil[kSearchWarps];
     // Sources of the current block, structure of arrays (16-byte aligned
     // rows so four consecutive sources load as one vector).
     __shared__ __align__(16) T source_x[kSearchWarps][32];
     __shared__ __align__(16) T source_y[kSearchWarps][32];
     __shared__ __align__(16) T source_z[kSearchWarps][32];
     __shared__ __align__(16) uint32_t source_key[kSearchWarps][32];
+    __shared__ int32_t source_atom[kSearchWarps][32];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     // Warp w serves bins w, w + stride, w + 2 stride, ...; it probes the
@@ -777,8 +858,9 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
         const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
         int32_t bx, by, bz;
         bin_coordinates(plan, bin, bx, by, bz);
-        StencilRows& rows = stencil[warp];
-        const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz, &rows, lane);
+        StencilRows<PairOnce>& rows = stencil[warp];
+        const int32_t total = load_stencil<PairOnce>(plan, args.bin_start, args.n_sources, bx, by, bz,
+                                                     &rows, lane);
         const int32_t words = (total + 31) >> 5;
         uint32_t* mask = args.mask_words + args.bin_word_start[bin];
         const T search2 = plan.search_squared;
@@ -805,16 +887,20 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 source_x[warp][lane] = q.x;
                 source_y[warp][lane] = q.y;
                 source_z[warp][lane] = q.z;
-                // Half lists: key(s) + 1; full lists: the atom.
-                source_key[warp][lane] = Half ? 2u * static_cast<uint32_t>(my_source) + 2u
-                                              : static_cast<uint32_t>(my_source);
-                const int32_t self = args.self_slot[my_source];
+                source_atom[warp][lane] = my_source;
+                // key(s) + 1 (keyed searches); the slot is the zero image's.
+                const uint32_t slot = first_source + base + lane;
+                source_key[warp][lane] = PairOnce ? 2u * slot + 2u
+                                                  : 2u * static_cast<uint32_t>(my_source) + 2u;
+                if constexpr (!PairOnce) {
 #pragma unroll
-                for (int r = 0; r < 9; ++r) {
-                    const int32_t begin_r = rows.prefix[r] + rows.delta[r];
-                    const int32_t length_r = rows.prefix[r + 1] - rows.prefix[r];
-                    if (self >= begin_r && self < begin_r + length_r) {
-                        self_k = rows.prefix[r] + (self - begin_r);
+                    for (int r = 0; r < StencilShape<false>::kZeroRanges; ++r) {
+                        const int32_t begin_r = rows.prefix[r] + rows.delta[r];
+                        const int32_t length_r = rows.prefix[r + 1] - rows.prefix[r];
+                        if (static_cast<int32_t>(slot) >= begin_r &&
+                            static_cast<int32_t>(slot) < begin_r + length_r) {
+                            self_k = rows.prefix[r] + (static_cast<int32_t>(slot) - begin_r);
+                        }
                     }
                 }
             } else if (lane < padded) {
@@ -868,7 +954,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                                                   sub2(d23, inner_pair));
                         search_signs = push_signs2(push_signs2(search_signs, sub2(d01, search_pair)),
                                                    sub2(d23, search_pair));
-                        if constexpr (Half) {
+                        if constexpr (Keyed) {
                             const uint4 k = *reinterpret_cast<const uint4*>(&source_key[warp][r0]);
                             key_signs = push_key(push_key(push_key(push_key(key_signs, k.x, key), k.y, key),
                                                           k.z, key), k.w, key);
@@ -880,14 +966,14 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                                                       source_y[warp][r], source_z[warp][r]);
                         inner_signs = push_sign(inner_signs, d2 - inner2);
                         search_signs = push_sign(search_signs, d2 - search2);
-                        if constexpr (Half) key_signs = push_key(key_signs, source_key[warp][r], key);
+                        if constexpr (Keyed) key_signs = push_key(key_signs, source_key[warp][r], key);
                     }
                 }
                 // Bit r: d2 to source r below the inner / search radius.
                 const uint32_t inside = __brev(inner_signs) >> (32 - padded);
                 const uint32_t near = __brev(search_signs) >> (32 - padded);
                 uint32_t keep_keys = valid_mask, band_keys = valid_mask;
-                if constexpr (Half) {
+                if constexpr (Keyed) {
                     keep_keys = band_keys = (__brev(key_signs) >> (32 - padded)) & valid_mask;
                     // key(c) == key(s) + 1: an image of source s itself, only
                     // possible where a lattice translation is shorter than the
@@ -907,14 +993,13 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                     do {
                         const int r = __ffs(rare) - 1;
                         rare &= rare - 1u;
-                        const uint32_t key_r = source_key[warp][r];
-                        const int32_t source = static_cast<int32_t>(Half ? (key_r - 2u) >> 1 : key_r);
+                        const int32_t source = source_atom[warp][r];
                         const long long shift[3] = {
                             meta.x + static_cast<long long>(args.wraps[3 * source]),
                             meta.y + static_cast<long long>(args.wraps[3 * source + 1]),
                             meta.z + static_cast<long long>(args.wraps[3 * source + 2])};
                         bool keep = true;
-                        if (Half && meta.w == source) keep = canonical_shift(shift);
+                        if (Keyed && meta.w == source) keep = canonical_shift(shift);
                         if (keep && !((inside >> r) & 1u)) {
                             const T* pt = args.positions + 3 * static_cast<int64_t>(meta.w);
                             const T vx = exact_component(pt[0], args.positions[3 * source], shift, plan.cell, 0);
@@ -930,7 +1015,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 const uint32_t my_word_bits = transpose_bits32(keep_bits, lane);
                 if (lane < block) {
                     uint32_t my_word = my_word_bits;
-                    if ((self_k >> 5) == w) {
+                    if (!PairOnce && (self_k >> 5) == w) {
                         const uint32_t bit = 1u << (self_k & 31);
                         my_word = args.include_self ? (my_word | bit) : (my_word & ~bit);
                     }
@@ -939,6 +1024,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 }
                 mask_out += n_sources;
             }
+            if (PairOnce) count = (Half ? count : 2u * count) + (args.include_self ? 1u : 0u);
             if (lane < block) {
                 args.counts[args.source_order ? static_cast<int64_t>(first_source + base + lane)
                                               : my_source] = count;
@@ -994,7 +1080,7 @@ __device__ __forceinline__ bool wants(const void* pointer, int bit) {
 
 template <typename T, int Q>
 __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const StructurePlan<T>& plan,
-                                            const StencilRows& rows, WriteShared<T>& sh,
+                                            WriteShared<T>& sh,
                                             int32_t n, int64_t out_row, int lane,
                                             bool need_shift, bool need_vector) {
     using V = vec4_t<T>;
@@ -1074,7 +1160,7 @@ __device__ __forceinline__ void flush_queue(const SearchArgs<T>& args, const Str
 template <typename T, int Q>
 __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
-    __shared__ StencilRows stencil[kSearchWarps];
+    __shared__ StencilRows<false> stencil[kSearchWarps];
     __shared__ WriteShared<T> shared[kSearchWarps];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1102,8 +1188,9 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
         const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
         int32_t bx, by, bz;
         bin_coordinates(plan, bin, bx, by, bz);
-        StencilRows& rows = stencil[warp];
-        const int32_t total = load_stencil(plan, args.bin_start, bx, by, bz, &rows, lane);
+        StencilRows<false>& rows = stencil[warp];
+        const int32_t total = load_stencil<false>(plan, args.bin_start, args.n_sources, bx, by, bz,
+                                                  &rows, lane);
         const int32_t words = (total + 31) >> 5;
         const uint32_t* bin_mask = args.mask_words + args.bin_word_start[bin];
         int64_t out_row = by_atom ? 0 : args.pair_start[first_source];
@@ -1166,7 +1253,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
                             sh.queue_k[lane] = slot_of(rows, 32 * item_w + bit);
                             sh.queue_r[lane] = static_cast<uint8_t>(item_r);
                         }
-                        flush_queue<T, Q>(args, plan, rows, sh, n, out_row + i, lane, need_shift,
+                        flush_queue<T, Q>(args, plan, sh, n, out_row + i, lane, need_shift,
                                     need_vector);
                     }
                     out_row += produced;
@@ -1189,12 +1276,20 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
 // round every busy lane takes one accepted candidate of its word, the ghost
 // records of that pair are loaded a round ahead, and the round's rows are
 // assigned by a ballot prefix so that each store covers one contiguous run.
+//
+// Unsorted calls are pair-once: the group's self pairs (include_self) come
+// first, then every accepted candidate gives one row in its canonical
+// orientation (half lists: the lower atom first, shifts and displacement
+// evaluated for that orientation) or two rows (full lists: both
+// orientations, the second half of each chunk holding the reversed rows).
+// Every displacement is the reference's public formula for the row's own
+// orientation, so a reversed row equals what the reference computes for it.
 constexpr int kEmitPerLane = 4;
 constexpr int kEmitQueue = 32 * kEmitPerLane;
 
 template <typename T>
 struct EmitShared {
-    StencilRows rows[32];
+    StencilRows<true> rows[32];
     // Per-source values as separate 4/8-byte arrays: lanes reading different
     // sources hit different banks.
     T pos[3][32];        // original source position
@@ -1208,7 +1303,47 @@ struct EmitShared {
 
 constexpr int kEmitThreads = 128;
 
+// Public displacement of one output row: (to - from) + S . cell in the
+// reference's operation order.
+template <typename T>
+__device__ __forceinline__ void row_vector(const T (&to)[3], const T (&from)[3],
+                                           const int32_t (&shift)[3], const T (&cell)[9],
+                                           T (&vec)[3]) {
+    const T s0 = static_cast<T>(shift[0]);
+    const T s1 = static_cast<T>(shift[1]);
+    const T s2 = static_cast<T>(shift[2]);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        vec[c] = add_rn(add_rn(add_rn(sub_rn(to[c], from[c]), mul_rn(s0, cell[c])),
+                               mul_rn(s1, cell[3 + c])), mul_rn(s2, cell[6 + c]));
+    }
+}
+
 template <typename T, int Q>
+__device__ __forceinline__ void store_row(const SearchArgs<T>& args, int64_t o, int64_t s,
+                                          int64_t t, const int32_t (&shift)[3],
+                                          const T (&vec)[3]) {
+    if (wants<Q>(args.out_i, kQ_I)) args.out_i[o] = s;
+    if (wants<Q>(args.out_j, kQ_J)) args.out_j[o] = t;
+    if (wants<Q>(args.out_P, kQ_P)) {
+        reinterpret_cast<longlong2*>(args.out_P)[o] = make_longlong2(s, t);
+    }
+    if (wants<Q>(args.out_S, kQ_S)) {
+        int32_t* row = args.out_S + 3 * o;
+        row[0] = shift[0];
+        row[1] = shift[1];
+        row[2] = shift[2];
+    }
+    if (wants<Q>(args.out_d, kQ_d)) args.out_d[o] = pair_distance(vec[0], vec[1], vec[2]);
+    if (wants<Q>(args.out_D, kQ_D)) {
+        T* row = args.out_D + 3 * o;
+        row[0] = vec[0];
+        row[1] = vec[1];
+        row[2] = vec[2];
+    }
+}
+
+template <typename T, int Q, bool Half>
 __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
     __shared__ EmitShared<T> shared[kEmitThreads / 32];
@@ -1236,29 +1371,9 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
             const StructurePlan<T>& plan = args.plans[args.bin_struct[bin]];
             int32_t bx, by, bz;
             bin_coordinates(plan, bin, bx, by, bz);
-            StencilRows& rows = sh.rows[lane];
-            int32_t prefix = 0;
-#pragma unroll
-            for (int r = 0; r < 9; ++r) {
-                int32_t begin = 0, length = 0;
-                const int32_t x = bx + r / 3 - 1;
-                const int32_t y = by + r % 3 - 1;
-                if (x >= 0 && x < plan.dims[0] && y >= 0 && y < plan.dims[1]) {
-                    const int32_t z0 = max(bz - 1, 0);
-                    const int32_t z1 = min(bz + 1, plan.dims[2] - 1);
-                    const int64_t row = plan.bin_begin +
-                        (static_cast<int64_t>(x) * plan.dims[1] + y) * plan.dims[2];
-                    begin = static_cast<int32_t>(args.bin_start[row + z0] & 0xffffffffull);
-                    length = static_cast<int32_t>(args.bin_start[row + z1 + 1] & 0xffffffffull) - begin;
-                }
-                rows.prefix[r] = prefix;
-                rows.delta[r] = begin - prefix;
-                prefix += length;
-            }
-            rows.prefix[9] = prefix;
-#pragma unroll
-            for (int r = 10; r < 16; ++r) rows.prefix[r] = INT_MAX;
-            words = (prefix + 31) >> 5;
+            const int32_t total = build_stencil<true>(plan, args.bin_start, args.n_sources, bx, by,
+                                                      bz, sh.rows[lane]);
+            words = (total + 31) >> 5;
             mask = args.mask_words + args.bin_word_start[bin] + (k - first);
             mask_stride = n_bin_sources;
 #pragma unroll
@@ -1285,6 +1400,17 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
         const int32_t batches = static_cast<int32_t>(__reduce_max_sync(kFullMask, static_cast<unsigned>(words)));
         __syncwarp();
         int64_t out_row = args.pair_start[group * 32];
+        if (args.include_self) {
+            // Zero-shift self pairs: (p - p) + 0 . cell is +0 in every component.
+            const unsigned valid_lanes = __ballot_sync(kFullMask, valid);
+            if (valid) {
+                const int64_t a = static_cast<int64_t>(sh.atom[lane]) + args.index_offset;
+                const int32_t zero_shift[3] = {0, 0, 0};
+                const T zero_vec[3] = {T(0), T(0), T(0)};
+                store_row<T, Q>(args, out_row + lane, a, a, zero_shift, zero_vec);
+            }
+            out_row += __popc(valid_lanes);
+        }
 
         // Word batches: lane l holds word `batch` of source l; the next batch
         // is loaded one batch ahead.  `avail`: nonzero words not yet taken.
@@ -1370,57 +1496,57 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
             for (int m = 0; m < kEmitPerLane; ++m) {
                 const int32_t e = lane + 32 * m;
                 if (e < queued) {
-                const int64_t o = out_row + e;
-                const int32_t r = source_r[m];
-                int32_t shift[3] = {0, 0, 0};
-                T vec[3] = {T(0), T(0), T(0)};
-                if (need_shift) {
-                    // Cell-list shifts fit int32 by construction of the plan.
-                    shift[0] = meta[m].x + sh.wrap[0][r];
-                    shift[1] = meta[m].y + sh.wrap[1][r];
-                    shift[2] = meta[m].z + sh.wrap[2][r];
-                }
-                if (need_vector) {
-                    V ps;
-                    ps.x = sh.pos[0][r];
-                    ps.y = sh.pos[1][r];
-                    ps.z = sh.pos[2][r];
+                    const int32_t r = source_r[m];
+                    int64_t a = sh.atom[r];
+                    int64_t b = meta[m].w;
+                    int32_t shift[3] = {0, 0, 0};
+                    if (need_shift) {
+                        // Cell-list shifts fit int32 by construction of the plan.
+                        shift[0] = meta[m].x + sh.wrap[0][r];
+                        shift[1] = meta[m].y + sh.wrap[1][r];
+                        shift[2] = meta[m].z + sh.wrap[2][r];
+                    }
+                    T pa[3] = {T(0), T(0), T(0)}, pb[3] = {T(0), T(0), T(0)};
                     T cell[9];
+                    if (need_vector) {
+                        pa[0] = sh.pos[0][r];
+                        pa[1] = sh.pos[1][r];
+                        pa[2] = sh.pos[2][r];
+                        pb[0] = pt[m].x;
+                        pb[1] = pt[m].y;
+                        pb[2] = pt[m].z;
 #pragma unroll
-                    for (int c = 0; c < 9; ++c) cell[c] = uniform_cell ? group_cell[c] : sh.cell[c][r];
-                    const T s0 = static_cast<T>(shift[0]);
-                    const T s1 = static_cast<T>(shift[1]);
-                    const T s2 = static_cast<T>(shift[2]);
-                    vec[0] = add_rn(add_rn(add_rn(sub_rn(pt[m].x, ps.x), mul_rn(s0, cell[0])),
-                                           mul_rn(s1, cell[3])), mul_rn(s2, cell[6]));
-                    vec[1] = add_rn(add_rn(add_rn(sub_rn(pt[m].y, ps.y), mul_rn(s0, cell[1])),
-                                           mul_rn(s1, cell[4])), mul_rn(s2, cell[7]));
-                    vec[2] = add_rn(add_rn(add_rn(sub_rn(pt[m].z, ps.z), mul_rn(s0, cell[2])),
-                                           mul_rn(s1, cell[5])), mul_rn(s2, cell[8]));
-                }
-                const int64_t s = static_cast<int64_t>(sh.atom[r]) + args.index_offset;
-                const int64_t t = static_cast<int64_t>(meta[m].w) + args.index_offset;
-                if (wants<Q>(args.out_i, kQ_I)) args.out_i[o] = s;
-                if (wants<Q>(args.out_j, kQ_J)) args.out_j[o] = t;
-                if (wants<Q>(args.out_P, kQ_P)) {
-                    reinterpret_cast<longlong2*>(args.out_P)[o] = make_longlong2(s, t);
-                }
-                if (wants<Q>(args.out_S, kQ_S)) {
-                    int32_t* row = args.out_S + 3 * o;
-                    row[0] = shift[0];
-                    row[1] = shift[1];
-                    row[2] = shift[2];
-                }
-                if (wants<Q>(args.out_d, kQ_d)) args.out_d[o] = pair_distance(vec[0], vec[1], vec[2]);
-                if (wants<Q>(args.out_D, kQ_D)) {
-                    T* row = args.out_D + 3 * o;
-                    row[0] = vec[0];
-                    row[1] = vec[1];
-                    row[2] = vec[2];
-                }
+                        for (int c = 0; c < 9; ++c) cell[c] = uniform_cell ? group_cell[c] : sh.cell[c][r];
+                    }
+                    // Half lists: canonical orientation, the lower atom first
+                    // (a == b is a periodic self image tested with its
+                    // canonical shift).
+                    if (Half && b < a) {
+                        const int64_t x = a;
+                        a = b;
+                        b = x;
+#pragma unroll
+                        for (int c = 0; c < 3; ++c) {
+                            shift[c] = -shift[c];
+                            const T y = pa[c];
+                            pa[c] = pb[c];
+                            pb[c] = y;
+                        }
+                    }
+                    T vec[3] = {T(0), T(0), T(0)};
+                    if (need_vector) row_vector(pb, pa, shift, cell, vec);
+                    store_row<T, Q>(args, out_row + e, a + args.index_offset, b + args.index_offset,
+                                    shift, vec);
+                    if constexpr (!Half) {
+#pragma unroll
+                        for (int c = 0; c < 3; ++c) shift[c] = -shift[c];
+                        if (need_vector) row_vector(pa, pb, shift, cell, vec);
+                        store_row<T, Q>(args, out_row + queued + e, b + args.index_offset,
+                                        a + args.index_offset, shift, vec);
+                    }
                 }
             }
-            out_row += queued;
+            out_row += Half ? queued : 2 * queued;
             queued = next_queued;
             current ^= 1;
         }
@@ -1992,7 +2118,11 @@ void launch_stencil_words(const SearchArgs<T>& args, unsigned long long* bin_wor
                           cudaStream_t stream) {
     if (args.n_bins == 0) return;
     const unsigned blocks = static_cast<unsigned>(blocks_for(args.n_bins, kBinThreads));
-    stencil_words_kernel<T><<<blocks, kBinThreads, 0, stream>>>(args, args.n_bins, bin_words);
+    if (args.pair_once) {
+        stencil_words_kernel<true, T><<<blocks, kBinThreads, 0, stream>>>(args, args.n_bins, bin_words);
+    } else {
+        stencil_words_kernel<false, T><<<blocks, kBinThreads, 0, stream>>>(args, args.n_bins, bin_words);
+    }
     ++g_kernel_launches;
 }
 
@@ -2018,23 +2148,31 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
                 default: launch(cell_write_kernel<T, 0>, needed); break;
             }
         } else {
-            switch (q) {
-                case kQ_P | kQ_S: launch(cell_emit_kernel<T, kQ_P | kQ_S>, groups, kEmitThreads); break;
-                case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
-                    launch(cell_emit_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D>, groups, kEmitThreads); break;
-                case kQ_P | kQ_S | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_S | kQ_D>, groups, kEmitThreads); break;
-                case kQ_P | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_D>, groups, kEmitThreads); break;
-                default: launch(cell_emit_kernel<T, 0>, groups, kEmitThreads); break;
-            }
+            auto emit = [&](auto half) {
+                constexpr bool H = decltype(half)::value;
+                switch (q) {
+                    case kQ_P | kQ_S: launch(cell_emit_kernel<T, kQ_P | kQ_S, H>, groups, kEmitThreads); break;
+                    case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
+                        launch(cell_emit_kernel<T, kQ_I | kQ_J | kQ_S | kQ_d | kQ_D, H>, groups, kEmitThreads); break;
+                    case kQ_P | kQ_S | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_S | kQ_D, H>, groups, kEmitThreads); break;
+                    case kQ_P | kQ_D: launch(cell_emit_kernel<T, kQ_P | kQ_D, H>, groups, kEmitThreads); break;
+                    default: launch(cell_emit_kernel<T, 0, H>, groups, kEmitThreads); break;
+                }
+            };
+            if (args.half_list) emit(std::true_type{}); else emit(std::false_type{});
         }
-    } else if (args.half_list) {
-        cell_count_kernel<T, true><<<persistent_blocks(cell_count_kernel<T, true>, kSearchThreads,
-                                                       needed), kSearchThreads, 0, stream>>>(args);
-    ++g_kernel_launches;
     } else {
-        cell_count_kernel<T, false><<<persistent_blocks(cell_count_kernel<T, false>, kSearchThreads,
-                                                        needed), kSearchThreads, 0, stream>>>(args);
-    ++g_kernel_launches;
+        auto count = [&](auto kernel) {
+            kernel<<<persistent_blocks(kernel, kSearchThreads, needed), kSearchThreads, 0, stream>>>(args);
+            ++g_kernel_launches;
+        };
+        if (args.pair_once) {
+            if (args.half_list) count(cell_count_kernel<T, true, true>);
+            else count(cell_count_kernel<T, false, true>);
+        } else {
+            if (args.half_list) count(cell_count_kernel<T, true, false>);
+            else count(cell_count_kernel<T, false, false>);
+        }
     }
 }
 

@@ -32,11 +32,13 @@ struct BinArgs {
     const int32_t* wraps;
     const void* wrapped;         // vec4_t<T>
     unsigned long long* bin_counts;  // histogram target / scatter cursors
+    int32_t pair_once;           // keep only copies a pair-once search can test
+    // Ghost arrays: zero images at [0, n_cell_atoms) in source-slot order,
+    // other image copies from n_cell_atoms on.
     void* ghost_pos;             // vec4_t<T> [G]   (scatter only)
     int4* ghost_meta;            // [G]             (scatter only)
     void* ghost_orig;            // vec4_t<T> [G]   (scatter only)
     const T* positions;
-    int32_t* self_slot;          // [N]             (scatter only)
     int32_t* source_list;        // [sources]       (scatter only)
     int32_t* source_bin;         // [sources]       (scatter only) bin of each listed source
     uint32_t* status;
@@ -55,13 +57,13 @@ struct SearchArgs {
     const unsigned long long* bin_start;
     const void* ghost_pos;  // vec4_t<T>
     const int4* ghost_meta;
-    const int32_t* self_slot;
-    int32_t* source_list;               // cell order; the count pass sorts each bin's 32-source blocks
+    int32_t* source_list;               // cell order (source slot -> atom)
     const int32_t* source_bin;          // [sources] bin of each source, cell order
     int64_t n_sources;
     const int32_t* bin_struct;          // [bins] structure of each bin
     const void* ghost_orig;             // vec4_t<T> [G] original target position, target
     int32_t source_order;               // 0: outputs by atom index; 1: cell order
+    int32_t pair_once;                  // each unordered pair tested from one side (cell order only)
     const int64_t* cell_bin_prefix;     // [n_cell + 1] first bin of each cell-list structure
     const int32_t* cell_structs;        // [n_cell]
     int32_t n_cell;

@@ -6,11 +6,12 @@
 //   atom_struct  int32 [N]          structure of each atom
 //   wraps        int32 [N][3]       floor(position . dual_T)  (reference wraps)
 //   wrapped      T4    [N]          position - wraps . cell, w unused
-//   bin_start    u64   [bins+1]     exclusive scan of (sources << 32 | ghosts)
-//   ghost_pos    T4    [G]          cell-sorted image copies (x, y, z, target)
+//   bin_start    u64   [bins+1]     exclusive scan of (sources << 32 | image copies)
+//   ghost_pos    T4    [G]          image copies (x, y, z, order key): the zero
+//                                   images at [0, S) by source slot, then the
+//                                   other copies cell-sorted from S on
 //   ghost_meta   int4  [G]          (image - wrap_target) xyz, target
-//   self_slot    int32 [N]          ghost slot of each atom's own zero image
-//   source_list  int32 [sources]    atoms of cell-list structures, cell-sorted
+//   source_list  int32 [S]          atoms of cell-list structures, cell-sorted
 //   pair_count   int32 [N]          pairs per source   -> pair_start int64 [N+1]
 // Outputs are written source-major at pair_start[source].
 #pragma once
