@@ -35,7 +35,8 @@ def neighbor_list(
     whose squared distance is strictly below ``cutoff**2``, for a batch of
     structures concatenated along ``batch_ptr``.  Returns a tuple with one
     tensor per character of ``quantities`` (``i j P S d D``), on the input
-    device.  Pairs are always source-major (``sorted`` is honoured for free).
+    device.  ``sorted=True`` returns pairs ordered by source; otherwise the
+    order is unspecified (cell order).
     See tonari src/tonari/api.py:66-174 for the full contract.
     """
     if not isinstance(quantities, str):

@@ -11,10 +11,11 @@
 //     -> scatter instead of per-bin linked lists, and never falls back to an
 //     O(N^2) pass because a wrap is nonzero: its final test is the public
 //     displacement formula, like the reference CPU cell list;
-//   * pairs are written source-major by construction, so `sorted` costs
-//     nothing and no argsort runs;
-//   * host round trips: at most three small device->host reads (per-structure
-//     extents, ghost total, pair total), each a pinned-memory copy.
+//   * sorted calls write each source's pairs at its own offset (no argsort);
+//     unsorted calls test each unordered pair once and write in cell order;
+//   * host round trips: at most four small device->host reads (input
+//     metadata, per-structure extents, ghost total, pair total), each a
+//     pinned-memory copy.
 #include "tonari_b200.h"
 
 #include <cuda_runtime.h>

@@ -909,6 +909,13 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 source_key[warp][lane] = 0u;
             }
             __syncwarp();
+            // Range of the block's key(s) + 1 values.
+            uint32_t block_key_lo = 0u, block_key_hi = 0u;
+            if constexpr (Keyed) {
+                const uint32_t mine = lane < block ? source_key[warp][lane] : 0u;
+                block_key_lo = __reduce_min_sync(kFullMask, lane < block ? mine : 0xffffffffu);
+                block_key_hi = __reduce_max_sync(kFullMask, mine);
+            }
             uint32_t count = 0;
             // This lane's candidate of tile w, loaded one tile ahead.  The
             // lane walks the stencil rows forward (k grows by 32 per tile):
@@ -938,9 +945,21 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                 const int32_t slot = next_slot;
                 if (w + 1 < words) load_candidate(w + 1, next, next_slot);
                 const uint32_t key = static_cast<uint32_t>(lane_to_index(cand.w));
-                uint32_t key_signs = 0;  // half lists: bit r = key(s_r) + 1 < key(c)
+                uint32_t key_signs = 0;  // keyed: bit r = key(s_r) + 1 < key(c)
                 uint32_t inner_signs = 0, search_signs = 0;
-                if constexpr (std::is_same<T, float>::value) {
+                // A tile whose candidates' keys all lie above or below the
+                // block's key(s) + 1 values needs no per-test key bit (a key
+                // equal to one of them is a periodic image of that source,
+                // which the keyed path flags).
+                bool keyed_tile = false;
+                uint32_t uniform_keys = 0u;
+                if constexpr (Keyed) {
+                    keyed_tile = __any_sync(kFullMask, key >= block_key_lo && key <= block_key_hi);
+                    uniform_keys = key > block_key_hi ? valid_mask : 0u;
+                }
+                auto tests = [&](auto with_keys) {
+                  constexpr bool KeyBits = decltype(with_keys)::value;
+                  if constexpr (std::is_same<T, float>::value) {
                     const unsigned long long cx = pack2(cand.x, cand.x);
                     const unsigned long long cy = pack2(cand.y, cand.y);
                     const unsigned long long cz = pack2(cand.z, cand.z);
@@ -954,31 +973,34 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
                                                   sub2(d23, inner_pair));
                         search_signs = push_signs2(push_signs2(search_signs, sub2(d01, search_pair)),
                                                    sub2(d23, search_pair));
-                        if constexpr (Keyed) {
+                        if constexpr (KeyBits) {
                             const uint4 k = *reinterpret_cast<const uint4*>(&source_key[warp][r0]);
                             key_signs = push_key(push_key(push_key(push_key(key_signs, k.x, key), k.y, key),
                                                           k.z, key), k.w, key);
                         }
                     }
-                } else {
+                  } else {
                     for (int r = 0; r < padded; ++r) {
                         const T d2 = screen_distance2(cand.x, cand.y, cand.z, source_x[warp][r],
                                                       source_y[warp][r], source_z[warp][r]);
                         inner_signs = push_sign(inner_signs, d2 - inner2);
                         search_signs = push_sign(search_signs, d2 - search2);
-                        if constexpr (Keyed) key_signs = push_key(key_signs, source_key[warp][r], key);
+                        if constexpr (KeyBits) key_signs = push_key(key_signs, source_key[warp][r], key);
                     }
-                }
+                  }
+                };
+                if (keyed_tile) tests(std::true_type{}); else tests(std::false_type{});
                 // Bit r: d2 to source r below the inner / search radius.
                 const uint32_t inside = __brev(inner_signs) >> (32 - padded);
                 const uint32_t near = __brev(search_signs) >> (32 - padded);
                 uint32_t keep_keys = valid_mask, band_keys = valid_mask;
                 if constexpr (Keyed) {
-                    keep_keys = band_keys = (__brev(key_signs) >> (32 - padded)) & valid_mask;
+                    keep_keys = band_keys = keyed_tile
+                        ? (__brev(key_signs) >> (32 - padded)) & valid_mask : uniform_keys;
                     // key(c) == key(s) + 1: an image of source s itself, only
                     // possible where a lattice translation is shorter than the
                     // search radius; its shift decides it in the rare path.
-                    if (self_images && (key & 1u) == 0u && key != 0u) {
+                    if (keyed_tile && self_images && (key & 1u) == 0u && key != 0u) {
                         for (int r = 0; r < block; ++r) {
                             if (source_key[warp][r] == key) band_keys |= 1u << r;
                         }
@@ -1346,6 +1368,7 @@ __device__ __forceinline__ void store_row(const SearchArgs<T>& args, int64_t o, 
 template <typename T, int Q, bool Half>
 __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
+    constexpr int PerLane = kEmitPerLane;
     __shared__ EmitShared<T> shared[kEmitThreads / 32];
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1452,12 +1475,12 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
         };
         // Selection rounds fill a queue of (slot, source) entries and need no
         // global loads but the staged mask words.  The queue is double
-        // buffered: the ghost records of chunk c (up to kEmitPerLane per
+        // buffered: the ghost records of chunk c (up to PerLane per
         // lane) are requested, the next chunk is selected while they are in
         // flight, and only then is chunk c computed and stored.
         auto fill = [&](int2* queue) -> int32_t {
             int32_t queued = 0;
-            while (queued <= kEmitQueue - 32) {
+            while (queued <= 32 * PerLane - 32) {
                 refill();
                 const bool has = bits != 0u;
                 const unsigned ballot = __ballot_sync(kFullMask, has);
@@ -1477,11 +1500,11 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
         int32_t queued = fill(sh.queue[0]);
         while (queued > 0) {
             const int2* queue = sh.queue[current];
-            int4 meta[kEmitPerLane];
-            V pt[kEmitPerLane];
-            int32_t source_r[kEmitPerLane];
+            int4 meta[PerLane];
+            V pt[PerLane];
+            int32_t source_r[PerLane];
 #pragma unroll
-            for (int m = 0; m < kEmitPerLane; ++m) {
+            for (int m = 0; m < PerLane; ++m) {
                 const int32_t e = lane + 32 * m;
                 source_r[m] = 0;
                 if (e < queued) {
@@ -1493,7 +1516,7 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
             }
             const int32_t next_queued = fill(sh.queue[current ^ 1]);
 #pragma unroll
-            for (int m = 0; m < kEmitPerLane; ++m) {
+            for (int m = 0; m < PerLane; ++m) {
                 const int32_t e = lane + 32 * m;
                 if (e < queued) {
                     const int32_t r = source_r[m];
