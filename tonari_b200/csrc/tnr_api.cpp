@@ -702,8 +702,9 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     bin_args.wrapped = d_wrapped;
     bin_args.status = d_status;
     // Unsorted calls test each unordered pair once (cell-order output);
-    // sorted calls search every source's full stencil.
-    const bool pair_once = !request.sorted;
+    // sorted calls search every source's full stencil.  Pair-once order keys
+    // are 2 * source slot + 2 < 2^31.
+    const bool pair_once = !request.sorted && n_cell_atoms < (int64_t{1} << 30) - 16;
     bin_args.pair_once = pair_once ? 1 : 0;
     const int64_t total_images = geometry.image_begin[batch];
     auto* d_image_shift = workspace.get<int4>(std::max<int64_t>(total_images, 1));

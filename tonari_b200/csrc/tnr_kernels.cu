@@ -393,11 +393,16 @@ __global__ void __launch_bounds__(kPrepareThreads) verify_wraps_kernel(
 // first so that the atom's other copies carry its source slot.
 //
 // Pair-once calls (args.pair_once) test every unordered pair from one side
-// only: from source s, candidate copy c of atom t is tested when
-// slot(t) > slot(s) (ties: the canonical shift).  Source slots follow the bin
-// order, so a copy whose atom's home bin lies below every bin of its own
-// stencil neighbourhood (bin - (d1 d2 + d2 + 1) in the row-major order) can
-// never be tested and is not kept.
+// only.  The pair (s, t) through image I of t's wrapped position is the pair
+// (t, s) through image -I of s's, so an image copy is kept only when its
+// image precedes the zero image in the x-major enumeration (its first nonzero
+// component is negative, the canonical shift rule), and every kept copy is
+// tested from every source near it.  Zero images (I = 0) are tested from the
+// source with the lower source slot.
+// Order key of a pair-once image copy: above every source's key(s) + 1
+// (2 slot + 2 < 2^31), so the key test accepts it for every source.
+constexpr uint32_t kImageCopyKey = 0x7ffffff0u;
+
 template <typename T, bool Scatter>
 __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
     using V = vec4_t<T>;
@@ -473,11 +478,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
             args.source_bin[source_slot] = static_cast<int32_t>(home);
         }
     }
-    // Pair-once: a copy in a bin above home + (d1 d2 + d2 + 1) has its atom's
-    // home below every bin of its stencil neighbourhood.
-    const int64_t highest_kept = args.pair_once
-        ? home + static_cast<int64_t>(dims[1]) * dims[2] + dims[2] + 1 : INT64_MAX;
-    for (int32_t k = 0; k < n_images; ++k) {
+    // Pair-once: images after the zero image are the reverses of kept ones.
+    const int32_t last_image = args.pair_once ? center : n_images;
+    const uint32_t image_key = args.pair_once ? kImageCopyKey : key_base + 2u;
+    for (int32_t k = 0; k < last_image; ++k) {
         if (k == center) continue;
         const V tr = translations[k];
         const T g[3] = {add_rn(q.x, tr.x), add_rn(q.y, tr.y), add_rn(q.z, tr.z)};
@@ -486,11 +490,10 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
                             g[2] >= lower[2] && g[2] <= upper[2];
         if (!inside) continue;
         const int64_t bin = bin_of(g);
-        if (bin > highest_kept) continue;
         const unsigned long long old = atomicAdd(&args.bin_counts[bin], 1ull);
         if constexpr (Scatter) {
             store(static_cast<uint32_t>(args.n_cell_atoms) + static_cast<uint32_t>(old & 0xffffffffull),
-                  g, k, key_base + 2u);
+                  g, k, image_key);
         }
     }
 }
@@ -2161,7 +2164,7 @@ void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stre
             kernel<<<persistent_blocks(kernel, threads, work), threads, 0, stream>>>(args);
             ++g_kernel_launches;
         };
-        if (args.source_order == 0) {
+        if (args.source_order == 0 || !args.pair_once) {
             switch (q) {
                 case kQ_P | kQ_S: launch(cell_write_kernel<T, kQ_P | kQ_S>, needed); break;
                 case kQ_I | kQ_J | kQ_S | kQ_d | kQ_D:
