@@ -56,6 +56,9 @@ constexpr int64_t kMaximumBinsPerImage = 64;
 // Total bins of one call (memory guard across a batch).
 constexpr int64_t kMaximumTotalBins = int64_t{1} << 28;
 constexpr int kRoundoffFactor = 64;
+// Calls whose ghost and bitmask bounds fit this much workspace size those
+// buffers from the bounds instead of reading the exact totals back.
+constexpr int64_t kBoundedWorkspaceBytes = int64_t{64} << 20;
 
 thread_local int64_t g_launches = 0;
 thread_local float g_phase_ms[6] = {0, 0, 0, 0, 0, 0};
@@ -698,6 +701,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     bin_args.cell_structs = reinterpret_cast<const int32_t*>(second_device + off_cell_structs);
     bin_args.n_cell = static_cast<int32_t>(cell_structs.size());
     bin_args.n_cell_atoms = n_cell_atoms;
+    for (int32_t b : cell_structs) bin_args.max_images = std::max(bin_args.max_images, plans[b].n_images);
     bin_args.wraps = d_wraps;
     bin_args.wrapped = d_wrapped;
     bin_args.status = d_status;
@@ -750,25 +754,50 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         launch_scan_u64(d_bin_words, total_bins, d_bin_word_start, nullptr, d_scan_workspace,
                         d_status, stream);
         check_launch("mask scan kernel");
-        unsigned long long packed_total = 0, mask_words = 0;
-        check_cuda(cudaMemcpyAsync(pinned_read, d_bin_start + total_bins, sizeof(packed_total),
-                                   cudaMemcpyDeviceToHost, stream), "read ghost total");
-        check_cuda(cudaMemcpyAsync(pinned_read + 8, d_bin_word_start + total_bins, sizeof(mask_words),
-                                   cudaMemcpyDeviceToHost, stream), "read mask words");
-        check_cuda(cudaStreamSynchronize(stream), "ghost total");
-        std::memcpy(&packed_total, pinned_read, sizeof(packed_total));
-        std::memcpy(&mask_words, pinned_read + 8, sizeof(mask_words));
-        timer.host(5);  // ghost and mask totals read back
-        require_search(mask_words < (1ull << 32), "cell-list candidate bitmask exceeds uint32 indexing");
-        d_mask_words = workspace.get<uint32_t>(mask_words);
-        // Ghost slots: the sources' zero images, then the other copies.
-        const int64_t sources = static_cast<int64_t>(packed_total >> 32);
-        const int64_t ghosts = sources + static_cast<int64_t>(packed_total & 0xffffffffull);
-        require_search(sources == n_cell_atoms && ghosts < std::numeric_limits<int32_t>::max(),
-                       "cell-list image copies exceed int32 indexing");
+        // Ghost and bitmask sizes.  Bounds from the plans: a structure of n
+        // atoms and I images places at most n (1 + (I - 1) / 2) copies
+        // (pair-once; n I otherwise), and a source's stencil holds at most
+        // its structure's copies.  Small calls allocate to those bounds and
+        // skip the read-back; the kernels check the capacities.
+        int64_t ghost_bound = 0, mask_bound = 0;
+        for (int32_t b : cell_structs) {
+            const int64_t images = plans[b].n_images;
+            const int64_t copies = counts[b] * (pair_once ? 1 + (images - 1) / 2 : images);
+            ghost_bound += copies;
+            mask_bound += counts[b] * ((copies + 31) / 32);
+        }
+        const int64_t ghost_record_bytes = static_cast<int64_t>(sizeof(V4) + sizeof(int4)) +
+            ((request.quantities & (TNR_Q_d | TNR_Q_D)) ? static_cast<int64_t>(sizeof(V4)) : 0);
+        const bool bounded = ghost_bound < std::numeric_limits<int32_t>::max() &&
+                             ghost_bound * ghost_record_bytes + mask_bound * 4 <= kBoundedWorkspaceBytes;
+        int64_t ghosts = ghost_bound;
+        unsigned long long mask_words = static_cast<unsigned long long>(mask_bound);
+        if (!bounded) {
+            unsigned long long packed_total = 0;
+            check_cuda(cudaMemcpyAsync(pinned_read, d_bin_start + total_bins, sizeof(packed_total),
+                                       cudaMemcpyDeviceToHost, stream), "read ghost total");
+            check_cuda(cudaMemcpyAsync(pinned_read + 8, d_bin_word_start + total_bins, sizeof(mask_words),
+                                       cudaMemcpyDeviceToHost, stream), "read mask words");
+            check_cuda(cudaStreamSynchronize(stream), "ghost total");
+            std::memcpy(&packed_total, pinned_read, sizeof(packed_total));
+            std::memcpy(&mask_words, pinned_read + 8, sizeof(mask_words));
+            timer.host(5);  // ghost and mask totals read back
+            require_search(mask_words < (1ull << 32), "cell-list candidate bitmask exceeds uint32 indexing");
+            // Ghost slots: the sources' zero images, then the other copies.
+            const int64_t sources = static_cast<int64_t>(packed_total >> 32);
+            ghosts = sources + static_cast<int64_t>(packed_total & 0xffffffffull);
+            require_search(sources == n_cell_atoms && ghosts < std::numeric_limits<int32_t>::max(),
+                           "cell-list image copies exceed int32 indexing");
+        }
+        d_mask_words = workspace.get<uint32_t>(std::max<unsigned long long>(mask_words, 1));
+        if (bounded) {
+            launch_capacity_check(d_bin_word_start + total_bins, mask_words, d_status, stream);
+            check_launch("capacity check kernel");
+        }
         d_ghost_pos = workspace.get<V4>(ghosts);
         d_ghost_meta = workspace.get<int4>(ghosts);
         if (request.quantities & (TNR_Q_d | TNR_Q_D)) d_ghost_orig = workspace.get<V4>(ghosts);
+        bin_args.ghost_capacity = ghosts;
         d_source_list = workspace.get<int32_t>(n_cell_atoms);
         d_source_bin = workspace.get<int32_t>(n_cell_atoms);
         bin_args.bin_counts = d_cursor;
@@ -841,7 +870,12 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         check_launch("brute count kernel");
     }
     timer.mark(3);
-    timer.host(6);  // count pass launched
+    // The pair-count scan is queued before the host's geometry check so
+    // that the device does not wait for it.
+    launch_scan_counts(d_counts, n_atoms, d_pair_start, d_scan_workspace, d_status, stream);
+    check_launch("pair scan kernel");
+    timer.mark(4);
+    timer.host(6);  // count pass and scan launched
     if (speculate) {
         // While the search runs: the exact geometry (the reference's long-
         // double arithmetic) must give the same T duals and image ranges as
@@ -867,9 +901,6 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                                d_exact_duals, d_wraps, d_status + 2, stream);
         check_launch("wrap check kernel");
     }
-    launch_scan_counts(d_counts, n_atoms, d_pair_start, d_scan_workspace, d_status, stream);
-    check_launch("pair scan kernel");
-    timer.mark(4);
     check_cuda(cudaMemcpyAsync(pinned_read, d_pair_start + n_atoms, sizeof(int64_t),
                                cudaMemcpyDeviceToHost, stream), "read pair total");
     check_cuda(cudaMemcpyAsync(pinned_read + sizeof(int64_t), d_status, 3 * sizeof(uint32_t),

@@ -161,7 +161,7 @@ PeriodicGeometry build_geometry(const double* cells, const uint8_t* pbc,
             }
         }
     };
-    HostPool::instance().parallel_for(batch, 128, run);
+    HostPool::instance().parallel_for(batch, 16, run);
     geometry.image_begin.assign(static_cast<size_t>(batch + 1), 0);
     for (int64_t b = 0; b < batch; ++b) {
         if (b == failed_at) throw InputError(failure);

@@ -390,7 +390,10 @@ __global__ void __launch_bounds__(kPrepareThreads) verify_wraps_kernel(
 // at [0, S) in source-slot order and the other image copies at [S, S + I).
 // Each bin counter packs (sources << 32 | image copies), so one 64-bit
 // atomic hands out the slot in either region.  The zero image is placed
-// first so that the atom's other copies carry its source slot.
+// first so that the atom's other copies carry its source slot.  When the
+// atoms alone cannot fill the GPU, gridDim.y > 1 threads share an atom's
+// images (thread y takes images y, y + gridDim.y, ...; y = 0 also places the
+// zero image); copies then depend on the atom only, not on its slot.
 //
 // Pair-once calls (args.pair_once) test every unordered pair from one side
 // only.  The pair (s, t) through image I of t's wrapped position is the pair
@@ -461,12 +464,11 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
                                           static_cast<int32_t>(atom));
     };
     // Zero image: the source.
-    int64_t home;
-    uint32_t key_base;  // order key base: 2 * (source slot or atom)
-    {
+    uint32_t key_base = 2u * static_cast<uint32_t>(atom);  // 2 * (source slot or atom)
+    if (blockIdx.y == 0) {
         const V tr = translations[center];
         const T g[3] = {add_rn(q.x, tr.x), add_rn(q.y, tr.y), add_rn(q.z, tr.z)};
-        home = bin_of(g);
+        const int64_t home = bin_of(g);
         const unsigned long long old = atomicAdd(&args.bin_counts[home], 1ull << 32);
         const uint32_t source_slot = static_cast<uint32_t>(old >> 32);
         key_base = 2u * (args.pair_once ? source_slot : static_cast<uint32_t>(atom));
@@ -481,7 +483,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
     // Pair-once: images after the zero image are the reverses of kept ones.
     const int32_t last_image = args.pair_once ? center : n_images;
     const uint32_t image_key = args.pair_once ? kImageCopyKey : key_base + 2u;
-    for (int32_t k = 0; k < last_image; ++k) {
+    for (int32_t k = blockIdx.y; k < last_image; k += gridDim.y) {
         if (k == center) continue;
         const V tr = translations[k];
         const T g[3] = {add_rn(q.x, tr.x), add_rn(q.y, tr.y), add_rn(q.z, tr.z)};
@@ -492,8 +494,12 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
         const int64_t bin = bin_of(g);
         const unsigned long long old = atomicAdd(&args.bin_counts[bin], 1ull);
         if constexpr (Scatter) {
-            store(static_cast<uint32_t>(args.n_cell_atoms) + static_cast<uint32_t>(old & 0xffffffffull),
-                  g, k, image_key);
+            const int64_t slot = args.n_cell_atoms + static_cast<int64_t>(old & 0xffffffffull);
+            if (slot >= args.ghost_capacity) {  // never, for a correct bound
+                atomicOr(args.status, static_cast<uint32_t>(kStatusCapacity));
+                continue;
+            }
+            store(static_cast<uint32_t>(slot), g, k, image_key);
         }
     }
 }
@@ -699,6 +705,23 @@ __device__ __forceinline__ int32_t slot_of(const StencilRows<PairOnce>& rows, in
 }
 
 
+// slot_of with the lane's current range cached: a new range is looked up only
+// when k passes range_end (0 forces a lookup).
+template <bool PairOnce>
+__device__ __forceinline__ int32_t cached_slot(const StencilRows<PairOnce>& rows, int32_t k,
+                                               int32_t& range_end, int32_t& range_delta) {
+    if (k >= range_end) {
+        int32_t r = 0;
+#pragma unroll
+        for (int step = StencilShape<PairOnce>::kTable / 2; step > 0; step >>= 1) {
+            r += (rows.prefix[r + step] <= k) ? step : 0;
+        }
+        range_end = rows.prefix[r + 1];
+        range_delta = rows.delta[r];
+    }
+    return k + range_delta;
+}
+
 // Per bin: bitmask words of all its sources (sources * ceil(candidates / 32)).
 // One thread per bin; its row-bound loads are independent.
 template <bool PairOnce, typename T>
@@ -836,6 +859,9 @@ __global__ void __launch_bounds__(kSearchThreads) cell_count_kernel(SearchArgs<T
     __shared__ __align__(16) T source_z[kSearchWarps][32];
     __shared__ __align__(16) uint32_t source_key[kSearchWarps][32];
     __shared__ int32_t source_atom[kSearchWarps][32];
+    // A bitmask sized from a bound that the scanned total exceeds (never,
+    // for a correct bound) is flagged before this pass: nothing is written.
+    if (*args.status & kStatusCapacity) return;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     // Warp w serves bins w, w + stride, w + 2 stride, ...; it probes the
@@ -1446,6 +1472,9 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
         unsigned avail = __ballot_sync(kFullMask, stage != 0u);
         uint32_t bits = 0;  // this lane's current word (untaken candidates)
         int32_t my_r = 0, my_w = 0;
+        // Stencil range of the lane's last candidate: candidates below
+        // range_end map to slot k + range_delta (bits are taken in order).
+        int32_t range_end = 0, range_delta = 0;
         auto refill = [&]() {
             while (true) {
                 const unsigned need = __ballot_sync(kFullMask, bits == 0u);
@@ -1471,6 +1500,7 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
                     bits = static_cast<uint32_t>(handed.x);
                     my_r = handed.y;
                     my_w = batch;
+                    range_end = 0;
                 }
                 avail = __ballot_sync(kFullMask, offering && offer_rank >= __popc(need));
                 __syncwarp();
@@ -1492,7 +1522,7 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
                     const int32_t bit = __ffs(bits) - 1;
                     bits &= bits - 1u;
                     queue[queued + __popc(ballot & below)] =
-                        make_int2(slot_of(sh.rows[my_r], 32 * my_w + bit), my_r);
+                        make_int2(cached_slot(sh.rows[my_r], 32 * my_w + bit, range_end, range_delta), my_r);
                 }
                 queued += __popc(ballot);
             }
@@ -2111,14 +2141,25 @@ void launch_prepare(const PrepareArgs<T>& args, cudaStream_t stream) {
 template <typename T>
 void launch_bin(const BinArgs<T>& args, bool scatter, cudaStream_t stream) {
     if (args.n_cell_atoms == 0) return;
-    const unsigned blocks = static_cast<unsigned>(blocks_for(args.n_cell_atoms, kBinThreads));
-    if (scatter) {
-        bin_kernel<T, true><<<blocks, kBinThreads, 0, stream>>>(args);
-    ++g_kernel_launches;
-    } else {
-        bin_kernel<T, false><<<blocks, kBinThreads, 0, stream>>>(args);
-    ++g_kernel_launches;
+    dim3 grid(static_cast<unsigned>(blocks_for(args.n_cell_atoms, kBinThreads)), 1, 1);
+    // Threads per atom: enough to reach about two full waves of the GPU when
+    // the atoms alone do not (small batches of structures with many images).
+    // Image copies depend on the atom only in pair-once calls (and on the
+    // atom index otherwise), so any split gives the same copies.
+    {
+        int device = 0, sms = 148;
+        cudaGetDevice(&device);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        const int64_t target = int64_t{sms} * 2048 * 2;
+        const int64_t split = std::min<int64_t>(args.max_images, target / std::max<int64_t>(args.n_cell_atoms, 1));
+        grid.y = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(split, 64)));
     }
+    if (scatter) {
+        bin_kernel<T, true><<<grid, kBinThreads, 0, stream>>>(args);
+    } else {
+        bin_kernel<T, false><<<grid, kBinThreads, 0, stream>>>(args);
+    }
+    ++g_kernel_launches;
 }
 
 template <typename T>
@@ -2136,6 +2177,17 @@ void launch_bin_struct(const int64_t* cell_bin_prefix, const int32_t* cell_struc
     if (n_cell == 0) return;
     bin_struct_kernel<<<static_cast<unsigned>(n_cell), 256, 0, stream>>>(cell_bin_prefix,
                                                                         cell_structs, bin_struct);
+    ++g_kernel_launches;
+}
+
+__global__ void capacity_check_kernel(const unsigned long long* total, unsigned long long capacity,
+                                      uint32_t* status) {
+    if (*total > capacity) atomicOr(status, static_cast<uint32_t>(kStatusCapacity));
+}
+
+void launch_capacity_check(const unsigned long long* total, unsigned long long capacity,
+                           uint32_t* status, cudaStream_t stream) {
+    capacity_check_kernel<<<1, 1, 0, stream>>>(total, capacity, status);
     ++g_kernel_launches;
 }
 

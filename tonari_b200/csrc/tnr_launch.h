@@ -29,10 +29,12 @@ struct BinArgs {
     const int32_t* cell_structs; // [n_cell]
     int32_t n_cell;
     int64_t n_cell_atoms;
+    int32_t max_images;          // largest image count of a cell-list structure
     const int32_t* wraps;
     const void* wrapped;         // vec4_t<T>
     unsigned long long* bin_counts;  // histogram target / scatter cursors
     int32_t pair_once;           // keep only copies a pair-once search can test
+    int64_t ghost_capacity;      // ghost slots allocated (scatter only)
     // Ghost arrays: zero images at [0, n_cell_atoms) in source-slot order,
     // other image copies from n_cell_atoms on.
     void* ghost_pos;             // vec4_t<T> [G]   (scatter only)
@@ -169,6 +171,10 @@ void launch_bin_struct(const int64_t* cell_bin_prefix, const int32_t* cell_struc
 template <typename T>
 void launch_stencil_words(const SearchArgs<T>& args, unsigned long long* bin_words,
                           cudaStream_t stream);
+
+// Sets the capacity status bit when *total exceeds capacity (one thread).
+void launch_capacity_check(const unsigned long long* total, unsigned long long capacity,
+                           uint32_t* status, cudaStream_t stream);
 
 template <typename T>
 void launch_cell_search(const SearchArgs<T>& args, bool write, cudaStream_t stream);
