@@ -934,6 +934,20 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     search.out_S = result.S;
     search.out_d = static_cast<T*>(result.d);
     search.out_D = static_cast<T*>(result.D);
+    {
+        // Full pair-once lists write both orientations of a pair as adjacent
+        // rows with 8- and 16-byte stores when every output is aligned for
+        // them (each source's row count is even, and include_self adds one
+        // row to each of the 32 sources of a write group, so every group
+        // starts at an even row).
+        auto aligned = [](const void* p, uintptr_t a) {
+            return reinterpret_cast<uintptr_t>(p) % a == 0;
+        };
+        search.paired_rows = (pair_once && !request.half_list && aligned(search.out_i, 16) &&
+                              aligned(search.out_j, 16) && aligned(search.out_P, 16) &&
+                              aligned(search.out_S, 8) && aligned(search.out_d, 2 * sizeof(T)) &&
+                              aligned(search.out_D, 2 * sizeof(T))) ? 1 : 0;
+    }
     timer.mark(5);
     if (q != 0) {
         if (n_cell_atoms) {

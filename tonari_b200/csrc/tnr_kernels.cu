@@ -1328,11 +1328,12 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
 // records of that pair are loaded a round ahead, and the round's rows are
 // assigned by a ballot prefix so that each store covers one contiguous run.
 //
-// Unsorted calls are pair-once: the group's self pairs (include_self) come
-// first, then every accepted candidate gives one row in its canonical
+// Unsorted calls are pair-once: every accepted candidate gives one row in its canonical
 // orientation (half lists: the lower atom first, shifts and displacement
 // evaluated for that orientation) or two rows (full lists: both
-// orientations, the second half of each chunk holding the reversed rows).
+// orientations, in adjacent rows or, when the outputs are not aligned for
+// that, in the two halves of each chunk); the group's self pairs
+// (include_self) come last.
 // Every displacement is the reference's public formula for the row's own
 // orientation, so a reversed row equals what the reference computes for it.
 constexpr int kEmitPerLane = 4;
@@ -1394,6 +1395,45 @@ __device__ __forceinline__ void store_row(const SearchArgs<T>& args, int64_t o, 
     }
 }
 
+// Both orientations of one full-list pair as adjacent rows o (even) and o + 1:
+// 16-byte index stores and 8- or 16-byte S, d and D stores (the host checks
+// the outputs' alignment; rows of a full list start at even offsets).
+template <typename T> struct Pair2;
+template <> struct Pair2<float> { using type = float2; };
+template <> struct Pair2<double> { using type = double2; };
+
+template <typename T, int Q>
+__device__ __forceinline__ void store_row_pair(const SearchArgs<T>& args, int64_t o, int64_t s,
+                                               int64_t t, const int32_t (&shift)[3],
+                                               const T (&vec)[3], const T (&back)[3]) {
+    using T2 = typename Pair2<T>::type;
+    if (wants<Q>(args.out_i, kQ_I)) *reinterpret_cast<longlong2*>(args.out_i + o) = make_longlong2(s, t);
+    if (wants<Q>(args.out_j, kQ_J)) *reinterpret_cast<longlong2*>(args.out_j + o) = make_longlong2(t, s);
+    if (wants<Q>(args.out_P, kQ_P)) {
+        longlong2* row = reinterpret_cast<longlong2*>(args.out_P) + o;
+        row[0] = make_longlong2(s, t);
+        row[1] = make_longlong2(t, s);
+    }
+    if (wants<Q>(args.out_S, kQ_S)) {
+        int2* row = reinterpret_cast<int2*>(args.out_S + 3 * o);
+        row[0] = make_int2(shift[0], shift[1]);
+        row[1] = make_int2(shift[2], -shift[0]);
+        row[2] = make_int2(-shift[1], -shift[2]);
+    }
+    if (wants<Q>(args.out_d, kQ_d)) {
+        // The reversed displacement has the same magnitudes component by
+        // component (round-to-nearest is sign-symmetric), so the same d.
+        const T d = pair_distance(vec[0], vec[1], vec[2]);
+        *reinterpret_cast<T2*>(args.out_d + o) = T2{d, d};
+    }
+    if (wants<Q>(args.out_D, kQ_D)) {
+        T2* row = reinterpret_cast<T2*>(args.out_D + 3 * o);
+        row[0] = T2{vec[0], vec[1]};
+        row[1] = T2{vec[2], back[0]};
+        row[2] = T2{back[1], back[2]};
+    }
+}
+
 template <typename T, int Q, bool Half>
 __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> args) {
     using V = vec4_t<T>;
@@ -1452,17 +1492,6 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
         const int32_t batches = static_cast<int32_t>(__reduce_max_sync(kFullMask, static_cast<unsigned>(words)));
         __syncwarp();
         int64_t out_row = args.pair_start[group * 32];
-        if (args.include_self) {
-            // Zero-shift self pairs: (p - p) + 0 . cell is +0 in every component.
-            const unsigned valid_lanes = __ballot_sync(kFullMask, valid);
-            if (valid) {
-                const int64_t a = static_cast<int64_t>(sh.atom[lane]) + args.index_offset;
-                const int32_t zero_shift[3] = {0, 0, 0};
-                const T zero_vec[3] = {T(0), T(0), T(0)};
-                store_row<T, Q>(args, out_row + lane, a, a, zero_shift, zero_vec);
-            }
-            out_row += __popc(valid_lanes);
-        }
 
         // Word batches: lane l holds word `batch` of source l; the next batch
         // is loaded one batch ahead.  `avail`: nonzero words not yet taken.
@@ -1591,20 +1620,39 @@ __global__ void __launch_bounds__(kEmitThreads) cell_emit_kernel(SearchArgs<T> a
                     }
                     T vec[3] = {T(0), T(0), T(0)};
                     if (need_vector) row_vector(pb, pa, shift, cell, vec);
-                    store_row<T, Q>(args, out_row + e, a + args.index_offset, b + args.index_offset,
-                                    shift, vec);
-                    if constexpr (!Half) {
-#pragma unroll
-                        for (int c = 0; c < 3; ++c) shift[c] = -shift[c];
-                        if (need_vector) row_vector(pa, pb, shift, cell, vec);
-                        store_row<T, Q>(args, out_row + queued + e, b + args.index_offset,
-                                        a + args.index_offset, shift, vec);
+                    if constexpr (Half) {
+                        store_row<T, Q>(args, out_row + e, a + args.index_offset,
+                                        b + args.index_offset, shift, vec);
+                    } else {
+                        const int32_t back_shift[3] = {-shift[0], -shift[1], -shift[2]};
+                        T back[3] = {T(0), T(0), T(0)};
+                        if (need_vector) row_vector(pa, pb, back_shift, cell, back);
+                        if (args.paired_rows) {
+                            store_row_pair<T, Q>(args, out_row + 2 * e, a + args.index_offset,
+                                                 b + args.index_offset, shift, vec, back);
+                        } else {
+                            store_row<T, Q>(args, out_row + e, a + args.index_offset,
+                                            b + args.index_offset, shift, vec);
+                            store_row<T, Q>(args, out_row + queued + e, b + args.index_offset,
+                                            a + args.index_offset, back_shift, back);
+                        }
                     }
                 }
             }
             out_row += Half ? queued : 2 * queued;
             queued = next_queued;
             current ^= 1;
+        }
+        if (args.include_self) {
+            // Zero-shift self pairs, after the group's other rows (so those
+            // start at the group's first row, which is even for full lists):
+            // (p - p) + 0 . cell is +0 in every component.
+            if (valid) {
+                const int64_t a = static_cast<int64_t>(sh.atom[lane]) + args.index_offset;
+                const int32_t zero_shift[3] = {0, 0, 0};
+                const T zero_vec[3] = {T(0), T(0), T(0)};
+                store_row<T, Q>(args, out_row + lane, a, a, zero_shift, zero_vec);
+            }
         }
         __syncwarp();
     }

@@ -66,6 +66,7 @@ struct SearchArgs {
     const void* ghost_orig;             // vec4_t<T> [G] original target position, target
     int32_t source_order;               // 0: outputs by atom index; 1: cell order
     int32_t pair_once;                  // each unordered pair tested from one side (cell order only)
+    int32_t paired_rows;                // full pair-once lists: both orientations in adjacent rows
     const int64_t* cell_bin_prefix;     // [n_cell + 1] first bin of each cell-list structure
     const int32_t* cell_structs;        // [n_cell]
     int32_t n_cell;
