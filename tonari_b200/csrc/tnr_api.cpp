@@ -111,12 +111,22 @@ public:
         void* pointer = raw(std::max<size_t>(count * sizeof(U), 16));
         return static_cast<U*>(pointer);
     }
+    // Buffers up to kCarveLimit bytes are carved (256-byte aligned) out of
+    // kChunkBytes chunks, so a call makes a few allocator round trips
+    // instead of one per small buffer; larger ones are allocated directly.
+    // Every chunk and buffer is released in stream order when the call ends.
     void* raw(size_t bytes) {
-        void* pointer = allocator_.allocate(allocator_.context, bytes,
-                                            reinterpret_cast<tnr_stream>(stream_));
-        if (pointer == nullptr) throw std::bad_alloc();
-        buffers_.push_back(pointer);
-        return pointer;
+        bytes = (bytes + 255) / 256 * 256;
+        if (bytes <= kCarveLimit) {
+            if (chunk_ == nullptr || chunk_used_ + bytes > kChunkBytes) {
+                chunk_ = static_cast<char*>(allocate(kChunkBytes));
+                chunk_used_ = 0;
+            }
+            void* pointer = chunk_ + chunk_used_;
+            chunk_used_ += bytes;
+            return pointer;
+        }
+        return allocate(bytes);
     }
     // Output buffers are not released by the workspace.
     template <typename U>
@@ -138,10 +148,21 @@ public:
     void keep_outputs() { outputs_.clear(); }
 
 private:
+    static constexpr size_t kCarveLimit = size_t{256} << 10;
+    static constexpr size_t kChunkBytes = size_t{4} << 20;
+    void* allocate(size_t bytes) {
+        void* pointer = allocator_.allocate(allocator_.context, bytes,
+                                            reinterpret_cast<tnr_stream>(stream_));
+        if (pointer == nullptr) throw std::bad_alloc();
+        buffers_.push_back(pointer);
+        return pointer;
+    }
     tnr_allocator allocator_;
     cudaStream_t stream_;
     std::vector<void*> buffers_;
     std::vector<void*> outputs_;
+    char* chunk_ = nullptr;
+    size_t chunk_used_ = 0;
 };
 
 // Pinned host staging, one growable buffer per host thread.  Every call

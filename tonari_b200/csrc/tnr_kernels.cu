@@ -35,6 +35,11 @@ constexpr int kPrepareThreads = 512;
 constexpr int kBinThreads = 256;
 constexpr int kSearchThreads = 256;
 constexpr int kSearchWarps = kSearchThreads / 32;
+// Bin kernels: six resident blocks per SM (40 registers) keep more of the
+// scatter's returned atomics in flight than four blocks at 56 registers.
+#ifndef TNR_BIN_MIN_BLOCKS
+#define TNR_BIN_MIN_BLOCKS 6
+#endif
 
 // ---------------------------------------------------------------------------
 // geometry (speculative, double precision)
@@ -407,7 +412,7 @@ __global__ void __launch_bounds__(kPrepareThreads) verify_wraps_kernel(
 constexpr uint32_t kImageCopyKey = 0x7ffffff0u;
 
 template <typename T, bool Scatter>
-__global__ void __launch_bounds__(kBinThreads) bin_kernel(BinArgs<T> args) {
+__global__ void __launch_bounds__(kBinThreads, TNR_BIN_MIN_BLOCKS) bin_kernel(BinArgs<T> args) {
     using V = vec4_t<T>;
     __shared__ int32_t block_first_last[2];
     const int64_t block_base = static_cast<int64_t>(blockIdx.x) * kBinThreads;
