@@ -308,12 +308,15 @@ def cpu_reference_rate(w, threads=None):
 # DRAM bytes (read + write) of the dominant kernel per emitted pair, keyed by
 # (workload, phase), from one ncu capture of that kernel on a reduced case of
 # the same workload; `traffic` scales it by the call's pairs.  Sources:
-#   cfg4 write pass: profiles/cell_emit_cfg4_200k.md (45.6 MB + 738.6 MB for
+#   cfg4 write pass: profiles/cell_emit_cfg4_200k.md (40.7 MB + 738.5 MB for
 #     18,104,094 pairs at 200,000 atoms);
-#   cfg5 count pass: profiles/cell_count_cfg5_512.md (49.3 MB + 2.1 MB for
-#     11,101,838 half pairs at 512 structures).
-TRAFFIC_PER_PAIR = {("cfg4", "write"): 784.189184e6 / 18_104_094,
-                    ("cfg5", "count"): 51.445248e6 / 11_101_838}
+#   cfg5 write pass: profiles/cell_emit_cfg5_1024.md (99.8 MB + 567.4 MB for
+#     22,354,478 half pairs at 1,024 structures);
+#   cfg5 count pass: profiles/cell_count_cfg5_1024.md (80.7 MB + 10.0 MB for
+#     the same 22,354,478 half pairs).
+TRAFFIC_PER_PAIR = {("cfg4", "write"): (40.664832e6 + 738.508032e6) / 18_104_094,
+                    ("cfg5", "write"): (99.836160e6 + 567.427328e6) / 22_354_478,
+                    ("cfg5", "count"): (80.659712e6 + 10.031104e6) / 22_354_478}
 
 
 def roofline(w, n_pairs, phase_ms, step_ms):
