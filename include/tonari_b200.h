@@ -90,7 +90,8 @@ typedef struct {
     uint32_t quantities;      /* OR of tnr_quantity */
     int64_t index_offset;     /* added to every emitted atom index (shards) */
     int32_t sorted;           /* bool: pairs ordered by source index; when false the
-                                 order is unspecified (cell order, faster writes) */
+                                 order is unspecified (each unordered pair is
+                                 searched once, faster) */
 } tnr_request;
 
 typedef struct {
@@ -109,7 +110,9 @@ typedef struct {
  * (positions, batch_ptr, cell, pbc, cutoff, half_list, include_self,
  * algorithm, sorted).  With request->sorted the pairs of each source are
  * contiguous and sources ascend; without it the order is unspecified, as in
- * the reference, and pairs are written in cell order (faster).
+ * the reference: each unordered pair is searched once and written where it
+ * was found, in its canonical orientation (half lists) or in both (full
+ * lists), which is faster.
  * Work is enqueued on `stream`; the call returns after the pair count is
  * known and the write pass has been enqueued (outputs are ready in stream
  * order).  On error `message` receives the reference's error text.

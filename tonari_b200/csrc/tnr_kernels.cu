@@ -1341,7 +1341,10 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
 // (include_self) come last.
 // Every displacement is the reference's public formula for the row's own
 // orientation, so a reversed row equals what the reference computes for it.
-constexpr int kEmitPerLane = 4;
+#ifndef TNR_EMIT_PER_LANE
+#define TNR_EMIT_PER_LANE 4
+#endif
+constexpr int kEmitPerLane = TNR_EMIT_PER_LANE;
 constexpr int kEmitQueue = 32 * kEmitPerLane;
 
 template <typename T>
