@@ -1342,7 +1342,7 @@ __global__ void __launch_bounds__(kSearchThreads) cell_write_kernel(SearchArgs<T
 // Every displacement is the reference's public formula for the row's own
 // orientation, so a reversed row equals what the reference computes for it.
 #ifndef TNR_EMIT_PER_LANE
-#define TNR_EMIT_PER_LANE 4
+#define TNR_EMIT_PER_LANE 6
 #endif
 constexpr int kEmitPerLane = TNR_EMIT_PER_LANE;
 constexpr int kEmitQueue = 32 * kEmitPerLane;
