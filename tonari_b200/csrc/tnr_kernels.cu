@@ -259,10 +259,14 @@ __global__ void __launch_bounds__(kPrepareThreads) prepare_kernel(PrepareArgs<T>
     const int64_t block_base = static_cast<int64_t>(blockIdx.x) * kPrepareThreads;
     const int64_t atom = block_base + threadIdx.x;
     const bool valid = atom < args.n_atoms;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {  // warp 0: 32-way searches, a few dependent loads
         const int64_t last = min(args.n_atoms - 1, block_base + kPrepareThreads - 1);
-        block_first_last[0] = structure_of(args.batch_ptr, args.batch, block_base);
-        block_first_last[1] = structure_of(args.batch_ptr, args.batch, last);
+        const int64_t first = warp_last_le(args.batch_ptr, 0, args.batch, block_base);
+        const int64_t closing = warp_last_le(args.batch_ptr, first, args.batch, last);
+        if (threadIdx.x == 0) {
+            block_first_last[0] = static_cast<int32_t>(first);
+            block_first_last[1] = static_cast<int32_t>(closing);
+        }
     }
     __syncthreads();
 
@@ -417,10 +421,14 @@ __global__ void __launch_bounds__(kBinThreads, TNR_BIN_MIN_BLOCKS) bin_kernel(Bi
     __shared__ int32_t block_first_last[2];
     const int64_t block_base = static_cast<int64_t>(blockIdx.x) * kBinThreads;
     const int64_t index = block_base + threadIdx.x;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {  // warp 0: 32-way searches, a few dependent loads
         const int64_t last = min(args.n_cell_atoms - 1, block_base + kBinThreads - 1);
-        block_first_last[0] = segment_of(args.cell_prefix, args.n_cell, block_base);
-        block_first_last[1] = segment_of(args.cell_prefix, args.n_cell, last);
+        const int64_t first = warp_last_le(args.cell_prefix, 0, args.n_cell, block_base);
+        const int64_t closing = warp_last_le(args.cell_prefix, first, args.n_cell, last);
+        if (threadIdx.x == 0) {
+            block_first_last[0] = static_cast<int32_t>(first);
+            block_first_last[1] = static_cast<int32_t>(closing);
+        }
     }
     __syncthreads();
     if (index >= args.n_cell_atoms) return;

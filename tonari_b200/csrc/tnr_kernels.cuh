@@ -142,4 +142,23 @@ __device__ __forceinline__ int32_t segment_of(const int64_t* __restrict__ prefix
     return lo;
 }
 
+// The same search by a whole warp (all 32 lanes call it with equal
+// arguments): the largest k in [lo, hi) with prefix[k] <= value, given
+// prefix[lo] <= value and prefix nondecreasing.  Each step narrows the range
+// 32-fold with one load per lane, so a block's first structure is found in
+// a few dependent loads instead of one per halving.
+__device__ __forceinline__ int64_t warp_last_le(const int64_t* __restrict__ prefix, int64_t lo,
+                                                int64_t hi, int64_t value) {
+    const int lane = threadIdx.x & 31;
+    while (hi - lo > 1) {
+        const int64_t step = (hi - lo + 31) / 32;
+        const int64_t k = lo + lane * step;
+        const bool le = k < hi && prefix[k] <= value;
+        const unsigned ballot = __ballot_sync(0xffffffffu, le);
+        lo += static_cast<int64_t>(31 - __clz(ballot)) * step;
+        hi = min(lo + step, hi);
+    }
+    return lo;
+}
+
 }  // namespace tnr
