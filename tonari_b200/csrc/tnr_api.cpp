@@ -496,28 +496,36 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     char* pinned_read = pinned + prepare_bytes + plan_bytes;
 
     // ---- prepare: wraps, wrapped positions, per-structure extents ---------
-    // Written straight into the pinned upload block by the host pool.
-    Upload first(pinned_prepare, prepare_bytes);
-    size_t off_prepare = 0, off_reduction = 0;
-    PrepareStructure<T>* prepare = first.place<PrepareStructure<T>>(static_cast<size_t>(batch), off_prepare);
-    Reduction<T>* neutral = first.place<Reduction<T>>(static_cast<size_t>(batch), off_reduction);
-    const Reduction<T> neutral_value = neutral_reduction<T>();
-    HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
-        for (int64_t b = begin; b < end; ++b) {
-            neutral[b] = neutral_value;
-            if (speculate) continue;  // the geometry kernel writes the prepare records
-            PrepareStructure<T>& st = prepare[b];
-            st.atom_begin = batch_ptr[b];
-            st.atom_end = batch_ptr[b + 1];
-            for (int k = 0; k < 9; ++k) {
-                st.cell[k] = cell_t[9 * b + k];
-                st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
+    // Host path: prepare records and neutral extents are written straight
+    // into the pinned upload block by the host pool.  Speculative geometry:
+    // the geometry kernel writes both on the device, and nothing is uploaded.
+    PrepareStructure<T>* d_prepare = nullptr;
+    Reduction<T>* d_reductions = nullptr;
+    if (speculate) {
+        d_prepare = workspace.get<PrepareStructure<T>>(static_cast<size_t>(batch));
+        d_reductions = workspace.get<Reduction<T>>(static_cast<size_t>(batch));
+    } else {
+        Upload first(pinned_prepare, prepare_bytes);
+        size_t off_prepare = 0, off_reduction = 0;
+        PrepareStructure<T>* prepare = first.place<PrepareStructure<T>>(static_cast<size_t>(batch), off_prepare);
+        Reduction<T>* neutral = first.place<Reduction<T>>(static_cast<size_t>(batch), off_reduction);
+        const Reduction<T> neutral_value = neutral_reduction<T>();
+        HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
+            for (int64_t b = begin; b < end; ++b) {
+                neutral[b] = neutral_value;
+                PrepareStructure<T>& st = prepare[b];
+                st.atom_begin = batch_ptr[b];
+                st.atom_end = batch_ptr[b + 1];
+                for (int k = 0; k < 9; ++k) {
+                    st.cell[k] = cell_t[9 * b + k];
+                    st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
+                }
             }
-        }
-    });
-    char* first_device = first.commit(workspace, stream);
-    auto* d_prepare = reinterpret_cast<PrepareStructure<T>*>(first_device + off_prepare);
-    auto* d_reductions = reinterpret_cast<Reduction<T>*>(first_device + off_reduction);
+        });
+        char* first_device = first.commit(workspace, stream);
+        d_prepare = reinterpret_cast<PrepareStructure<T>*>(first_device + off_prepare);
+        d_reductions = reinterpret_cast<Reduction<T>*>(first_device + off_reduction);
+    }
 
     int64_t* d_batch_ptr = const_cast<int64_t*>(request.batch_ptr);
     if (d_batch_ptr == nullptr) {
@@ -532,7 +540,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     if (speculate) {
         d_geometry = workspace.get<DeviceGeometry>(batch);
         launch_geometry<T>(static_cast<const T*>(request.cell), request.pbc, d_batch_ptr, batch,
-                           request.cutoff, d_prepare, d_geometry, d_status + 1, stream);
+                           request.cutoff, d_prepare, d_geometry, d_status + 1, d_reductions, stream);
         check_launch("geometry kernel");
     }
 

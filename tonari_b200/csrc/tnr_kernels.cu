@@ -53,9 +53,22 @@ template <typename T>
 __global__ void geometry_kernel(const T* __restrict__ cell, const uint8_t* __restrict__ pbc,
                                 const int64_t* __restrict__ batch_ptr, int64_t batch, double cutoff,
                                 PrepareStructure<T>* __restrict__ prepare,
-                                DeviceGeometry* __restrict__ out, uint32_t* flags) {
+                                DeviceGeometry* __restrict__ out, uint32_t* flags,
+                                Reduction<T>* __restrict__ reductions) {
     const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (b >= batch) return;
+    {
+        // The prepare kernel's extents start from the neutral element.
+        Reduction<T> neutral{};
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            neutral.wrapped_min[c] = order_key(static_cast<T>(INFINITY));
+            neutral.wrapped_max[c] = order_key(static_cast<T>(-INFINITY));
+            neutral.position_abs_max[c] = order_key(T(0));
+            neutral.wrap_abs_max[c] = 0;
+        }
+        reductions[b] = neutral;
+    }
     const double eps = 2.220446049250313e-16;  // double epsilon
     double c[9];
     bool bad = false;
@@ -2177,10 +2190,10 @@ void launch_filter(const FilterArgs<T>& args, bool write, cudaStream_t stream) {
 template <typename T>
 void launch_geometry(const T* cell, const uint8_t* pbc, const int64_t* batch_ptr, int64_t batch,
                      double cutoff, PrepareStructure<T>* prepare, DeviceGeometry* geometry,
-                     uint32_t* flags, cudaStream_t stream) {
+                     uint32_t* flags, Reduction<T>* reductions, cudaStream_t stream) {
     if (batch == 0) return;
     geometry_kernel<T><<<static_cast<unsigned>(blocks_for(batch, 128)), 128, 0, stream>>>(
-        cell, pbc, batch_ptr, batch, cutoff, prepare, geometry, flags);
+        cell, pbc, batch_ptr, batch, cutoff, prepare, geometry, flags, reductions);
     ++g_kernel_launches;
 }
 
@@ -2388,6 +2401,7 @@ void launch_scan_counts(const uint32_t* in, int64_t n, int64_t* out, void* works
                                          const int32_t*, uint32_t*, cudaStream_t);            \
     template void launch_geometry<T>(const T*, const uint8_t*, const int64_t*, int64_t, double, \
                                      PrepareStructure<T>*, DeviceGeometry*, uint32_t*,         \
+                                     Reduction<T>*,                                            \
                                      cudaStream_t);                                            \
     template void launch_bin<T>(const BinArgs<T>&, bool, cudaStream_t);                     \
     template void launch_image_table<T>(const StructurePlan<T>*, int64_t, int4*, void*,    \

@@ -116,7 +116,7 @@ struct DeviceGeometry {
 template <typename T>
 void launch_geometry(const T* cell, const uint8_t* pbc, const int64_t* batch_ptr, int64_t batch,
                      double cutoff, PrepareStructure<T>* prepare, DeviceGeometry* geometry,
-                     uint32_t* flags, cudaStream_t stream);
+                     uint32_t* flags, Reduction<T>* reductions, cudaStream_t stream);
 
 // Candidate-pair filter (Verlet-skin reuse): one bit per candidate, set when
 // its exact public-formula distance is below the cutoff.
