@@ -59,6 +59,9 @@ constexpr int kRoundoffFactor = 64;
 // Calls whose ghost and bitmask bounds fit this much workspace size those
 // buffers from the bounds instead of reading the exact totals back.
 constexpr int64_t kBoundedWorkspaceBytes = int64_t{64} << 20;
+// Calls of at least this many atoms run the speculative wrap check on a side
+// stream beside the search.
+constexpr int64_t kSideStreamAtoms = 500000;
 
 thread_local int64_t g_launches = 0;
 thread_local float g_phase_ms[6] = {0, 0, 0, 0, 0, 0};
@@ -192,6 +195,28 @@ private:
 };
 
 thread_local Pinned g_pinned;
+
+// A second stream (per host thread and device) for work that can overlap the
+// call's main stream, with the two events that fork and join it.  Like every
+// launch of this library it assumes the current device is the stream's.
+struct SideStream {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr;
+    cudaEvent_t join = nullptr;
+};
+
+SideStream& side_stream() {
+    thread_local SideStream streams[64];
+    int device = 0;
+    check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+    SideStream& side = streams[device & 63];
+    if (side.stream == nullptr) {
+        check_cuda(cudaStreamCreateWithFlags(&side.stream, cudaStreamNonBlocking), "side stream");
+        check_cuda(cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming), "fork event");
+        check_cuda(cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming), "join event");
+    }
+    return side;
+}
 
 // Packs several host arrays into a caller-provided pinned region (256-byte
 // aligned offsets) and uploads them with a single copy.
@@ -549,6 +574,12 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
                                 d_reductions, d_status};
     launch_prepare(prepare_args, stream);
     check_launch("prepare kernel");
+    // The wrap check (speculative geometry) forks here: it needs only the
+    // prepare kernel's wraps and runs beside the search on a side stream.
+    // Small calls keep it on the main stream, where it costs less than the
+    // fork and join.
+    SideStream* side = speculate && n_atoms >= kSideStreamAtoms ? &side_stream() : nullptr;
+    if (side) check_cuda(cudaEventRecord(side->fork, stream), "fork record");
     timer.host(2);  // prepare launched
     timer.mark(1);
 
@@ -924,11 +955,19 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         T* exact_duals = reinterpret_cast<T*>(pinned_prepare);
         for (int64_t k = 0; k < 9 * batch; ++k) exact_duals[k] = static_cast<T>(exact.duals[k]);
         T* d_exact_duals = workspace.get<T>(9 * batch);
+        const cudaStream_t check_stream = side ? side->stream : stream;
+        if (side) check_cuda(cudaStreamWaitEvent(side->stream, side->fork, 0), "fork wait");
         check_cuda(cudaMemcpyAsync(d_exact_duals, exact_duals, 9 * batch * sizeof(T),
-                                   cudaMemcpyHostToDevice, stream), "upload exact duals");
+                                   cudaMemcpyHostToDevice, check_stream), "upload exact duals");
         launch_verify_wraps<T>(static_cast<const T*>(request.positions), n_atoms, d_atom_struct,
-                               d_exact_duals, d_wraps, d_status + 2, stream);
+                               d_exact_duals, d_wraps, d_status + 2, check_stream);
         check_launch("wrap check kernel");
+        if (side) {
+            // Join before the status read-back (and before the workspace, the
+            // exact duals included, is released on the main stream).
+            check_cuda(cudaEventRecord(side->join, side->stream), "join record");
+            check_cuda(cudaStreamWaitEvent(stream, side->join, 0), "join wait");
+        }
     }
     check_cuda(cudaMemcpyAsync(pinned_read, d_pair_start + n_atoms, sizeof(int64_t),
                                cudaMemcpyDeviceToHost, stream), "read pair total");

@@ -351,11 +351,33 @@ __global__ void __launch_bounds__(kPrepareThreads) prepare_kernel(PrepareArgs<T>
     // form contiguous runs; min/max are idempotent, so overlapping windows of
     // the doubling shuffle are harmless.
     const int lane = threadIdx.x & 31;
+    // A warp of one structure (the common case) reduces each 32-bit key with
+    // one redux instruction; warps that straddle structures, and 64-bit keys,
+    // take the segmented shuffle.
+    const int32_t lane0_sid = __shfl_sync(kFullMask, sid, 0);
+    const bool one_structure = __all_sync(kFullMask, sid >= 0 && sid == lane0_sid);
+    auto segmented = [&]() {
 #pragma unroll
-    for (int offset = 1; offset < 32; offset <<= 1) {
-        const int32_t other_sid = __shfl_down_sync(kFullMask, sid, offset);
-        const Extents<K> other = shfl_down(ext, offset);
-        if (lane + offset < 32 && other_sid == sid) combine(ext, other);
+        for (int offset = 1; offset < 32; offset <<= 1) {
+            const int32_t other_sid = __shfl_down_sync(kFullMask, sid, offset);
+            const Extents<K> other = shfl_down(ext, offset);
+            if (lane + offset < 32 && other_sid == sid) combine(ext, other);
+        }
+    };
+    if constexpr (std::is_same<K, int32_t>::value) {
+        if (one_structure) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                ext.lo[c] = __reduce_min_sync(kFullMask, ext.lo[c]);
+                ext.hi[c] = __reduce_max_sync(kFullMask, ext.hi[c]);
+                ext.abs_position[c] = __reduce_max_sync(kFullMask, ext.abs_position[c]);
+                ext.abs_wrap[c] = __reduce_max_sync(kFullMask, ext.abs_wrap[c]);
+            }
+        } else {
+            segmented();
+        }
+    } else {
+        segmented();
     }
     const int32_t previous_sid = __shfl_up_sync(kFullMask, sid, 1);
     const bool head = sid >= 0 && (lane == 0 || previous_sid != sid);
