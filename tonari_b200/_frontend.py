@@ -66,19 +66,6 @@ def validate_torch_inputs(positions, cell, pbc, cutoff, batch_ptr) -> None:
         raise ValueError("cutoff must be finite and positive")
 
 
-def public_displacements(positions: Tensor, cell: Tensor, batch_ptr: Tensor,
-                         pairs: Tensor, shifts: Tensor) -> Tensor:
-    """D = pos[j] - pos[i] + S @ cell[b(i)]  (src/tonari/_torch_frontend.py:89-104)."""
-    source = pairs[:, 0]
-    target = pairs[:, 1]
-    pair_batch = torch.bucketize(source.contiguous(), batch_ptr[1:], right=True)
-    return (
-        positions[target]
-        - positions[source]
-        + torch.einsum("ei,eij->ej", shifts.to(positions.dtype), cell[pair_batch])
-    )
-
-
 class _KernelDisplacements(torch.autograd.Function):
     """D from the kernel in the forward; the analytic gradient of the
     reference formula D = pos[j] - pos[i] + S @ cell[b(i)]
