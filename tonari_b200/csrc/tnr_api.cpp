@@ -454,6 +454,31 @@ bool speculate_geometry(const tnr_request& request) {
     return !(flag && flag[0] == '1');
 }
 
+// Host arrays of one call, kept per host thread and per element type so that
+// consecutive calls reuse their memory: freshly allocated arrays of a large
+// batch cost a page fault per 4 KB on first touch (about 0.1 ms for 8,192
+// structures).  run() binds each to a local reference, which the host pool's
+// lambdas capture, so worker threads read the calling thread's arrays.
+template <typename T>
+struct HostArrays {
+    std::vector<int64_t> batch_ptr;
+    std::vector<T> cell;
+    std::vector<uint8_t> pbc;
+    std::vector<int64_t> counts;
+    std::vector<double> cell64;
+    std::vector<int32_t> mode;
+    std::vector<CellPlan> outcomes;
+    std::vector<int32_t> cell_structs, brute_structs;
+    std::vector<int64_t> cell_prefix, brute_prefix, cell_bin_prefix;
+    PeriodicGeometry geometry;
+};
+
+template <typename T>
+HostArrays<T>& host_arrays() {
+    thread_local HostArrays<T> arrays;
+    return arrays;
+}
+
 template <typename T>
 void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
          tnr_result& result, bool speculate) {
@@ -463,9 +488,13 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     PhaseTimer timer(stream);
 
     // ---- host metadata (tonari csrc/torch/bindings_cuda.cpp:96-131) -------
-    std::vector<int64_t> batch_ptr(static_cast<size_t>(batch + 1));
-    std::vector<T> cell_t(static_cast<size_t>(9 * batch));
-    std::vector<uint8_t> pbc(static_cast<size_t>(3 * batch));
+    HostArrays<T>& arrays = host_arrays<T>();
+    std::vector<int64_t>& batch_ptr = arrays.batch_ptr;
+    std::vector<T>& cell_t = arrays.cell;
+    std::vector<uint8_t>& pbc = arrays.pbc;
+    batch_ptr.resize(static_cast<size_t>(batch + 1));
+    cell_t.resize(static_cast<size_t>(9 * batch));
+    pbc.resize(static_cast<size_t>(3 * batch));
     if (request.batch_ptr_host && request.cell_host && request.pbc_host) {
         std::memcpy(batch_ptr.data(), request.batch_ptr_host, batch_ptr.size() * sizeof(int64_t));
         std::memcpy(cell_t.data(), request.cell_host, cell_t.size() * sizeof(T));
@@ -489,15 +518,20 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     require_input(batch_ptr[0] == 0, "batch_ptr must start at zero");
     require_input(batch_ptr[batch] == n_atoms, "batch_ptr must end at N_total");
     timer.host(0);  // metadata on the host
-    std::vector<int64_t> counts(static_cast<size_t>(batch));
+    std::vector<int64_t>& counts = arrays.counts;
+    counts.resize(static_cast<size_t>(batch));
     for (int64_t b = 0; b < batch; ++b) {
         require_input(batch_ptr[b + 1] >= batch_ptr[b], "batch_ptr must be nondecreasing");
         counts[b] = batch_ptr[b + 1] - batch_ptr[b];
     }
     for (uint8_t& flag : pbc) flag = flag ? 1 : 0;
-    std::vector<double> cell64(cell_t.begin(), cell_t.end());
-    PeriodicGeometry geometry;
+    // The host geometry works on float64 cells.  Under speculation it runs
+    // only for the check beside the count pass, so the widening (about
+    // 0.1 ms for 8,192 cells) waits until then.
+    std::vector<double>& cell64 = arrays.cell64;
+    PeriodicGeometry& geometry = arrays.geometry;
     if (!speculate) {
+        cell64.assign(cell_t.begin(), cell_t.end());
         geometry = build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
     }
     timer.host(1);  // periodic geometry (host path)
@@ -619,6 +653,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         check_cuda(cudaMemcpyAsync(pinned_read + geometry_offset, d_geometry,
                                    static_cast<size_t>(batch) * sizeof(DeviceGeometry),
                                    cudaMemcpyDeviceToHost, stream), "read geometry");
+        HostPool::instance().prewake();  // the plans are built right after the wait
         check_cuda(cudaStreamSynchronize(stream), "extents");
         reductions = reinterpret_cast<const Reduction<T>*>(pinned_read);
         uint32_t status[2] = {0, 0};
@@ -640,8 +675,10 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     // Plans are built in place in the pinned upload block by the host pool;
     // without speculation this overlaps the prepare kernel, and the cell
     // plans, which need the extents, follow the read-back.
-    std::vector<int32_t> mode(static_cast<size_t>(batch), kModeEmpty);
-    std::vector<CellPlan> outcomes(static_cast<size_t>(batch), CellPlan::kUnsafe);
+    std::vector<int32_t>& mode = arrays.mode;
+    std::vector<CellPlan>& outcomes = arrays.outcomes;
+    mode.assign(static_cast<size_t>(batch), kModeEmpty);
+    outcomes.assign(static_cast<size_t>(batch), CellPlan::kUnsafe);
     Upload second(pinned_plan, plan_bytes);
     size_t off_plans = 0;
     StructurePlan<T>* plans = second.place<StructurePlan<T>>(static_cast<size_t>(batch), off_plans);
@@ -720,8 +757,14 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
 
     timer.host(11);  // bins laid out
     // ---- work lists -------------------------------------------------------
-    std::vector<int32_t> cell_structs, brute_structs;
-    std::vector<int64_t> cell_prefix{0}, brute_prefix{0};
+    std::vector<int32_t>& cell_structs = arrays.cell_structs;
+    std::vector<int32_t>& brute_structs = arrays.brute_structs;
+    std::vector<int64_t>& cell_prefix = arrays.cell_prefix;
+    std::vector<int64_t>& brute_prefix = arrays.brute_prefix;
+    cell_structs.clear();
+    brute_structs.clear();
+    cell_prefix.assign(1, 0);
+    brute_prefix.assign(1, 0);
     for (int64_t b = 0; b < batch; ++b) {
         if (mode[b] == kModeCell) {
             cell_structs.push_back(static_cast<int32_t>(b));
@@ -733,7 +776,8 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     }
     const int64_t n_cell_atoms = cell_prefix.back();
     const int64_t n_brute_atoms = brute_prefix.back();
-    std::vector<int64_t> cell_bin_prefix;
+    std::vector<int64_t>& cell_bin_prefix = arrays.cell_bin_prefix;
+    cell_bin_prefix.clear();
     for (int32_t b : cell_structs) cell_bin_prefix.push_back(plans[b].bin_begin);
     cell_bin_prefix.push_back(total_bins);
     const size_t off_cell_prefix = second.add(cell_prefix.data(), cell_prefix.size());
@@ -941,6 +985,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
         // double arithmetic) must give the same T duals and image ranges as
         // the device, else the call is repeated on the host path.  Its input
         // errors are raised by that repeat, in the reference's order.
+        cell64.assign(cell_t.begin(), cell_t.end());
         const PeriodicGeometry exact =
             build_geometry(cell64.data(), pbc.data(), counts.data(), batch, request.cutoff);
         for (int64_t b = 0; b < batch; ++b) {

@@ -59,6 +59,21 @@ public:
         body_ = nullptr;
     }
 
+    // Wakes the workers without work, so that they poll (instead of
+    // sleeping) when a parallel loop follows shortly: a caller about to
+    // block on the device calls this first, and the loop after the wait
+    // does not pay the threads' wake-up latency.
+    void prewake() {
+        if (workers_.empty()) return;
+        std::lock_guard<std::mutex> call(call_mutex_);
+        {
+            std::lock_guard<std::mutex> lock(mutex_);
+            body_ = nullptr;
+            generation_.fetch_add(1, std::memory_order_release);
+        }
+        wake_.notify_all();
+    }
+
     HostPool(const HostPool&) = delete;
     HostPool& operator=(const HostPool&) = delete;
 
@@ -95,8 +110,8 @@ private:
     void loop() {
         uint64_t seen = generation_.load(std::memory_order_acquire);
         for (;;) {
-            // Poll for up to 200 us, then sleep until the next generation.
-            const auto poll_until = std::chrono::steady_clock::now() + std::chrono::microseconds(200);
+            // Poll for up to 500 us, then sleep until the next generation.
+            const auto poll_until = std::chrono::steady_clock::now() + std::chrono::microseconds(500);
             while (generation_.load(std::memory_order_acquire) == seen &&
                    std::chrono::steady_clock::now() < poll_until) {
                 std::this_thread::yield();
