@@ -212,6 +212,30 @@ def test_rejects_invalid_batch_ptr(batch_ptr, message):
             torch.tensor(batch_ptr))
 
 
+@pytest.mark.parametrize(("edit", "message"),
+                         [("first", "start at zero"), ("last", "end at N_total"),
+                          ("order", "nondecreasing")])
+def test_rejects_invalid_batch_ptr_speculative_batch(edit, message):
+    # 64 float32 structures take the device geometry, whose kernels are queued
+    # before the host has read batch_ptr; the errors and their order are the
+    # reference's all the same (tests/backends/test_cuda_runtime.py:256-275).
+    b = 64
+    batch_ptr = torch.arange(0, 2 * b + 1, 2)
+    if edit == "first":
+        batch_ptr[0] = 1
+    elif edit == "last":
+        batch_ptr[-1] = 2 * b - 1
+    else:
+        batch_ptr[5], batch_ptr[6] = 12, 9
+    cell = 10.0 * torch.eye(3).expand(b, 3, 3).contiguous()
+    with pytest.raises(ValueError, match=message):
+        run(torch.rand((2 * b, 3)), cell, torch.ones((b, 3), dtype=torch.bool), 1.0, batch_ptr)
+    # The stream stays usable: a valid call right after.
+    batch_ptr = torch.arange(0, 2 * b + 1, 2)
+    pairs, _ = run(torch.rand((2 * b, 3)), cell, torch.ones((b, 3), dtype=torch.bool), 1.0, batch_ptr)
+    assert pairs.shape[1] == 2
+
+
 def test_sparse_layout_auto_and_forced():
     # tests/backends/test_algorithms.py:161-174; test_cuda_runtime.py:278-288
     positions = torch.zeros((256, 3))

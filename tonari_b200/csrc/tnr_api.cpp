@@ -203,6 +203,7 @@ struct SideStream {
     cudaStream_t stream = nullptr;
     cudaEvent_t fork = nullptr;
     cudaEvent_t join = nullptr;
+    cudaEvent_t metadata = nullptr;  // the call's metadata copy has landed
 };
 
 SideStream& side_stream() {
@@ -214,6 +215,7 @@ SideStream& side_stream() {
         check_cuda(cudaStreamCreateWithFlags(&side.stream, cudaStreamNonBlocking), "side stream");
         check_cuda(cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming), "fork event");
         check_cuda(cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming), "join event");
+        check_cuda(cudaEventCreateWithFlags(&side.metadata, cudaEventDisableTiming), "metadata event");
     }
     return side;
 }
@@ -487,7 +489,70 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     const int64_t batch = request.n_structures;
     PhaseTimer timer(stream);
 
+    // One pinned block for every later upload and readback of this call.
+    const size_t prepare_bytes = static_cast<size_t>(batch) *
+        (sizeof(PrepareStructure<T>) + sizeof(Reduction<T>)) + 1024;
+    const size_t plan_bytes = static_cast<size_t>(batch) *
+        (sizeof(StructurePlan<T>) + 3 * sizeof(int64_t) + 2 * sizeof(int32_t)) +
+        8192;
+    const size_t read_bytes =
+        static_cast<size_t>(batch) * (sizeof(Reduction<T>) + sizeof(DeviceGeometry)) + 2048;
+    const size_t block_bytes = prepare_bytes + plan_bytes + read_bytes;
+
+    // Device work of the first phase: wraps, wrapped positions and extents
+    // (prepare kernel), after the speculative geometry kernel when the
+    // geometry is speculated.  Host path: prepare records and neutral
+    // extents are uploaded from the pinned block first.
+    PrepareStructure<T>* d_prepare = nullptr;
+    Reduction<T>* d_reductions = nullptr;
+    int32_t* d_atom_struct = nullptr;
+    int32_t* d_wraps = nullptr;
+    V4* d_wrapped = nullptr;
+    uint32_t* d_status = nullptr;
+    DeviceGeometry* d_geometry = nullptr;
+    SideStream* side = nullptr;
+    int64_t* d_batch_ptr = const_cast<int64_t*>(request.batch_ptr);
+    bool launched = false;
+    auto launch_first_phase = [&]() {
+        if (d_batch_ptr == nullptr) {
+            throw InputError("batch_ptr device pointer is required");
+        }
+        if (speculate) {
+            d_prepare = workspace.get<PrepareStructure<T>>(static_cast<size_t>(batch));
+            d_reductions = workspace.get<Reduction<T>>(static_cast<size_t>(batch));
+        }
+        d_atom_struct = workspace.get<int32_t>(n_atoms);
+        d_wraps = workspace.get<int32_t>(3 * n_atoms);
+        d_wrapped = workspace.get<V4>(n_atoms);
+        d_status = workspace.get<uint32_t>(4);
+        check_cuda(cudaMemsetAsync(d_status, 0, 4 * sizeof(uint32_t), stream), "memset status");
+        if (speculate) {
+            d_geometry = workspace.get<DeviceGeometry>(batch);
+            launch_geometry<T>(static_cast<const T*>(request.cell), request.pbc, d_batch_ptr, batch,
+                               request.cutoff, d_prepare, d_geometry, d_status + 1, d_reductions, stream);
+            check_launch("geometry kernel");
+        }
+        PrepareArgs<T> prepare_args{static_cast<const T*>(request.positions), n_atoms, d_batch_ptr,
+                                    batch, d_prepare, d_atom_struct, d_wraps, d_wrapped,
+                                    d_reductions, d_status};
+        launch_prepare(prepare_args, stream);
+        check_launch("prepare kernel");
+        // The wrap check (speculative geometry) forks here: it needs only the
+        // prepare kernel's wraps and runs beside the search on a side stream.
+        // Small calls keep it on the main stream, where it costs less than the
+        // fork and join.
+        side = speculate && n_atoms >= kSideStreamAtoms ? &side_stream() : nullptr;
+        if (side) check_cuda(cudaEventRecord(side->fork, stream), "fork record");
+        launched = true;
+    };
+
     // ---- host metadata (tonari csrc/torch/bindings_cuda.cpp:96-131) -------
+    // Speculative geometry needs no host metadata to start: its kernels read
+    // batch_ptr, cell and pbc on the device, so they are queued right behind
+    // the metadata copy and run while the host waits for it and plans.  The
+    // host checks batch_ptr afterwards, with the reference's messages and
+    // order; the kernels stay within bounds for any batch_ptr that starts at
+    // zero, and the prepare kernel does nothing for one that does not.
     HostArrays<T>& arrays = host_arrays<T>();
     std::vector<int64_t>& batch_ptr = arrays.batch_ptr;
     std::vector<T>& cell_t = arrays.cell;
@@ -495,6 +560,7 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     batch_ptr.resize(static_cast<size_t>(batch + 1));
     cell_t.resize(static_cast<size_t>(9 * batch));
     pbc.resize(static_cast<size_t>(3 * batch));
+    char* pinned = nullptr;
     if (request.batch_ptr_host && request.cell_host && request.pbc_host) {
         std::memcpy(batch_ptr.data(), request.batch_ptr_host, batch_ptr.size() * sizeof(int64_t));
         std::memcpy(cell_t.data(), request.cell_host, cell_t.size() * sizeof(T));
@@ -502,7 +568,12 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
     } else {
         const size_t b0 = batch_ptr.size() * sizeof(int64_t);
         const size_t b1 = (cell_t.size() * sizeof(T) + 15) / 16 * 16;
-        char* staging = g_pinned.reserve(b0 + b1 + pbc.size() + 64);
+        const size_t staging_bytes = b0 + b1 + pbc.size() + 64;
+        const bool early = speculate && n_atoms > 0;
+        // Early launch: the staging area follows the call's block, which is
+        // then reserved once, before any copy into it is queued.
+        char* staging = early ? (pinned = g_pinned.reserve(block_bytes + staging_bytes)) + block_bytes
+                              : g_pinned.reserve(staging_bytes);
         check_cuda(cudaMemcpyAsync(staging, request.batch_ptr, b0, cudaMemcpyDeviceToHost, stream), "read batch_ptr");
         if (batch) {
             check_cuda(cudaMemcpyAsync(staging + b0, request.cell, cell_t.size() * sizeof(T),
@@ -510,7 +581,15 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
             check_cuda(cudaMemcpyAsync(staging + b0 + b1, request.pbc, pbc.size(),
                                        cudaMemcpyDeviceToHost, stream), "read pbc");
         }
-        check_cuda(cudaStreamSynchronize(stream), "metadata read");
+        if (early) {
+            SideStream& events = side_stream();
+            check_cuda(cudaEventRecord(events.metadata, stream), "metadata record");
+            timer.mark(0);
+            launch_first_phase();
+            check_cuda(cudaEventSynchronize(events.metadata), "metadata read");
+        } else {
+            check_cuda(cudaStreamSynchronize(stream), "metadata read");
+        }
         std::memcpy(batch_ptr.data(), staging, b0);
         std::memcpy(cell_t.data(), staging + b0, cell_t.size() * sizeof(T));
         std::memcpy(pbc.data(), staging + b0 + b1, pbc.size());
@@ -538,82 +617,40 @@ void run(const tnr_request& request, Workspace& workspace, cudaStream_t stream,
 
     result.n_pairs = 0;
     if (n_atoms == 0) return;
-    timer.mark(0);
-
-    // One pinned block for every later upload and readback of this call; it
-    // is reserved once here, after the metadata copy above has completed.
-    const size_t prepare_bytes = static_cast<size_t>(batch) *
-        (sizeof(PrepareStructure<T>) + sizeof(Reduction<T>)) + 1024;
-    const size_t plan_bytes = static_cast<size_t>(batch) *
-        (sizeof(StructurePlan<T>) + 3 * sizeof(int64_t) + 2 * sizeof(int32_t)) +
-        8192;
-    const size_t read_bytes =
-        static_cast<size_t>(batch) * (sizeof(Reduction<T>) + sizeof(DeviceGeometry)) + 2048;
-    char* pinned = g_pinned.reserve(prepare_bytes + plan_bytes + read_bytes);
+    if (!launched) {
+        timer.mark(0);
+        // Reserved after the metadata copy above has completed.
+        pinned = g_pinned.reserve(block_bytes);
+    }
     char* pinned_prepare = pinned;
     char* pinned_plan = pinned + prepare_bytes;
     char* pinned_read = pinned + prepare_bytes + plan_bytes;
 
-    // ---- prepare: wraps, wrapped positions, per-structure extents ---------
-    // Host path: prepare records and neutral extents are written straight
-    // into the pinned upload block by the host pool.  Speculative geometry:
-    // the geometry kernel writes both on the device, and nothing is uploaded.
-    PrepareStructure<T>* d_prepare = nullptr;
-    Reduction<T>* d_reductions = nullptr;
-    if (speculate) {
-        d_prepare = workspace.get<PrepareStructure<T>>(static_cast<size_t>(batch));
-        d_reductions = workspace.get<Reduction<T>>(static_cast<size_t>(batch));
-    } else {
-        Upload first(pinned_prepare, prepare_bytes);
-        size_t off_prepare = 0, off_reduction = 0;
-        PrepareStructure<T>* prepare = first.place<PrepareStructure<T>>(static_cast<size_t>(batch), off_prepare);
-        Reduction<T>* neutral = first.place<Reduction<T>>(static_cast<size_t>(batch), off_reduction);
-        const Reduction<T> neutral_value = neutral_reduction<T>();
-        HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
-            for (int64_t b = begin; b < end; ++b) {
-                neutral[b] = neutral_value;
-                PrepareStructure<T>& st = prepare[b];
-                st.atom_begin = batch_ptr[b];
-                st.atom_end = batch_ptr[b + 1];
-                for (int k = 0; k < 9; ++k) {
-                    st.cell[k] = cell_t[9 * b + k];
-                    st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
+    if (!launched) {
+        if (!speculate) {
+            Upload first(pinned_prepare, prepare_bytes);
+            size_t off_prepare = 0, off_reduction = 0;
+            PrepareStructure<T>* prepare = first.place<PrepareStructure<T>>(static_cast<size_t>(batch), off_prepare);
+            Reduction<T>* neutral = first.place<Reduction<T>>(static_cast<size_t>(batch), off_reduction);
+            const Reduction<T> neutral_value = neutral_reduction<T>();
+            HostPool::instance().parallel_for(batch, 1024, [&](int64_t begin, int64_t end) {
+                for (int64_t b = begin; b < end; ++b) {
+                    neutral[b] = neutral_value;
+                    PrepareStructure<T>& st = prepare[b];
+                    st.atom_begin = batch_ptr[b];
+                    st.atom_end = batch_ptr[b + 1];
+                    for (int k = 0; k < 9; ++k) {
+                        st.cell[k] = cell_t[9 * b + k];
+                        st.dual[k] = static_cast<T>(geometry.duals[9 * b + k]);
+                    }
                 }
-            }
-        });
-        char* first_device = first.commit(workspace, stream);
-        d_prepare = reinterpret_cast<PrepareStructure<T>*>(first_device + off_prepare);
-        d_reductions = reinterpret_cast<Reduction<T>*>(first_device + off_reduction);
+            });
+            char* first_device = first.commit(workspace, stream);
+            d_prepare = reinterpret_cast<PrepareStructure<T>*>(first_device + off_prepare);
+            d_reductions = reinterpret_cast<Reduction<T>*>(first_device + off_reduction);
+        }
+        launch_first_phase();
     }
-
-    int64_t* d_batch_ptr = const_cast<int64_t*>(request.batch_ptr);
-    if (d_batch_ptr == nullptr) {
-        throw InputError("batch_ptr device pointer is required");
-    }
-    auto* d_atom_struct = workspace.get<int32_t>(n_atoms);
-    auto* d_wraps = workspace.get<int32_t>(3 * n_atoms);
-    auto* d_wrapped = workspace.get<V4>(n_atoms);
-    auto* d_status = workspace.get<uint32_t>(4);
-    check_cuda(cudaMemsetAsync(d_status, 0, 4 * sizeof(uint32_t), stream), "memset status");
-    DeviceGeometry* d_geometry = nullptr;
-    if (speculate) {
-        d_geometry = workspace.get<DeviceGeometry>(batch);
-        launch_geometry<T>(static_cast<const T*>(request.cell), request.pbc, d_batch_ptr, batch,
-                           request.cutoff, d_prepare, d_geometry, d_status + 1, d_reductions, stream);
-        check_launch("geometry kernel");
-    }
-
-    PrepareArgs<T> prepare_args{static_cast<const T*>(request.positions), n_atoms, d_batch_ptr,
-                                batch, d_prepare, d_atom_struct, d_wraps, d_wrapped,
-                                d_reductions, d_status};
-    launch_prepare(prepare_args, stream);
-    check_launch("prepare kernel");
-    // The wrap check (speculative geometry) forks here: it needs only the
-    // prepare kernel's wraps and runs beside the search on a side stream.
-    // Small calls keep it on the main stream, where it costs less than the
-    // fork and join.
-    SideStream* side = speculate && n_atoms >= kSideStreamAtoms ? &side_stream() : nullptr;
-    if (side) check_cuda(cudaEventRecord(side->fork, stream), "fork record");
     timer.host(2);  // prepare launched
     timer.mark(1);
 

@@ -269,6 +269,10 @@ __global__ void __launch_bounds__(kPrepareThreads) prepare_kernel(PrepareArgs<T>
     __shared__ int32_t block_first_last[2];
     __shared__ Extents<K> warp_partial[kPrepareThreads / 32];
 
+    // The host may check batch_ptr only after this kernel was queued: the
+    // block searches below stay in bounds for any batch_ptr that starts at
+    // zero; for one that does not, nothing is done and the host reports it.
+    if (args.batch_ptr[0] != 0) return;
     const int64_t block_base = static_cast<int64_t>(blockIdx.x) * kPrepareThreads;
     const int64_t atom = block_base + threadIdx.x;
     const bool valid = atom < args.n_atoms;
